@@ -1,0 +1,624 @@
+// Non-causal attention forward O = softmax(Q K^T / sqrt(D)) V for sm_100a.
+//
+// Computes what the reference's warp-specialised Hopper kernels compute
+// (tuning/attn_test.cu:50-523 attnWS2StageBaselineKernel, :526-1055,
+// :1058-1580), with the reference's tail semantics (key columns >= S masked
+// before the softmax, tuning/attn_test.cu:152-170), built on Blackwell units:
+//
+//   * one TMA producer warp loads the Q tile(s) once and streams K and V tiles
+//     through a STAGES-deep ring of 128B-swizzled shared-memory slots guarded
+//     by full/empty mbarrier pairs;
+//   * one MMA warp (a single elected lane) issues tcgen05.mma:
+//       S_i = Q_i K_j^T    (A, B from shared memory, D in TMEM, f32)
+//       O_i += P_i V_j     (A = P read from TMEM, B = V from shared memory)
+//     and signals completion with tcgen05.commit onto mbarriers;
+//   * NQ softmax warpgroups (one per 128-row Q tile; thread t owns row t, which
+//     is TMEM lane t) read S with tcgen05.ld, run the online softmax in fp32
+//     with exp2 on the MUFU unit, write P (f16/bf16) back into TMEM over the S
+//     columns, and rescale O in TMEM only when the running row max grew by
+//     more than RESCALE_THRESHOLD (log2 units) -- the lazy correction step;
+//   * the same warpgroups finish the tile: O / rowsum, convert, stage in the
+//     (now free) Q shared-memory slot with the TMA 128B swizzle, TMA store.
+//
+// BM = 128 * NQ rows of Q per CTA.  With NQ = 2 the two softmax warpgroups
+// ping-pong: while one runs exp2 on its S tile the tensor core runs the other
+// tile's P V and next Q K^T.  With NQ = 1 the S accumulator is double-buffered
+// in TMEM when it fits (2 * BN + D <= 512 columns) so Q K_{j+1}^T overlaps the
+// softmax of tile j.
+//
+// Every wait is bounded (see wait_bar): on expiry the kernel records an error
+// code in a device status word, raises a CTA-local abort flag so the other
+// roles stop waiting, drains its own outstanding tensor-core work and returns.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace attnprof {
+
+// Status codes written by the kernel (the first error wins).  The host maps
+// them to ATTNPROF_ERR_DEVICE_TIMEOUT.
+enum : int {
+  kSiteQ = 1,
+  kSiteKvFull = 2,
+  kSiteKvEmpty = 3,
+  kSiteSFull = 4,
+  kSitePReady = 5,
+  kSiteODone = 6,
+  kSiteDrain = 7,
+  kDeviceTimeoutBase = 0x7100,
+};
+
+// Phase profiler layout (one designated CTA): [phase][slot][begin,end] u64
+// clock64 stamps, the first kProfSlots KV iterations.  The phases are those of
+// the reference's profiler (attn.cu:5-22): LoadQ, LoadK, LoadV, GEMM-QK,
+// SOFTMAX, GEMM-PV.
+constexpr int kProfPhases = 6;
+constexpr int kProfSlots = 32;
+enum : int { kPhLoadQ = 0, kPhLoadK = 1, kPhLoadV = 2, kPhQK = 3, kPhSoftmax = 4, kPhPV = 5 };
+
+struct AttnParams {
+  int S;                       // logical sequence length (rows of Q and of K/V per head)
+  int num_kv_tiles;            // ceil(S / BN)
+  float scale_log2;            // log2(e) / sqrt(D)
+  int* status;                 // device status word (0 = ok)
+  unsigned long long timeout_ns;
+  int fault_mode;              // 0 normal; 1 = producer never loads K/V (test of bounded waits)
+  unsigned long long* prof;    // PROFILE builds: stamp buffer, may be null
+  int prof_cta;                // linear CTA index to profile
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <typename T, int D_, int BN_, int NQ_, int STAGES_>
+struct AttnConfig {
+  static constexpr int D = D_;
+  static constexpr int BN = BN_;
+  static constexpr int NQ = NQ_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+
+  static_assert(D == 64 || D == 128, "head dim must be 64 or 128");
+  static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN must be 32/64/128/256");
+  static_assert(NQ == 1 || NQ == 2, "NQ must be 1 or 2");
+  static_assert(STAGES >= 2, "need at least two K/V slots");
+
+  static constexpr int QROWS = 128;  // rows per Q tile = MMA M = TMEM lanes
+  static constexpr int BM = QROWS * NQ;
+  static constexpr int DBLK = D / 64;  // 64-element (128 B) column blocks per row
+
+  // TMEM columns (32-bit each).  S_i (and P_i over it) then O_i.
+  static constexpr int NSBUF = (NQ == 1 && 2 * BN + D <= 512) ? 2 : 1;
+  static constexpr int TMEM_S_COLS = NQ * NSBUF * BN;
+  static constexpr int TMEM_O_COL = TMEM_S_COLS;
+  static constexpr int TMEM_USED = TMEM_S_COLS + NQ * D;
+  static_assert(TMEM_USED <= 512, "tile does not fit in tensor memory");
+  static constexpr int TMEM_ALLOC = TMEM_USED <= 32    ? 32
+                                    : TMEM_USED <= 64  ? 64
+                                    : TMEM_USED <= 128 ? 128
+                                    : TMEM_USED <= 256 ? 256
+                                                       : 512;
+
+  // Shared memory (offsets from a 1024-byte aligned base).
+  static constexpr int Q_TILE_BYTES = QROWS * D * 2;
+  static constexpr int Q_BLK_BYTES = QROWS * 128;
+  static constexpr int KV_TILE_BYTES = BN * D * 2;
+  static constexpr int KV_BLK_BYTES = BN * 128;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = OFF_Q + NQ * Q_TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE_BYTES;
+
+  static constexpr int BAR_Q = 0;
+  static constexpr int BAR_KV_FULL = BAR_Q + NQ;
+  static constexpr int BAR_KV_EMPTY = BAR_KV_FULL + STAGES;
+  static constexpr int BAR_S_FULL = BAR_KV_EMPTY + STAGES;  // [NQ][NSBUF]
+  static constexpr int BAR_P_READY = BAR_S_FULL + NQ * NSBUF;
+  static constexpr int BAR_O_DONE = BAR_P_READY + NQ;
+  static constexpr int BAR_DRAIN = BAR_O_DONE + NQ;
+  static constexpr int NUM_BARS = BAR_DRAIN + 1;
+
+  static constexpr int OFF_MISC = OFF_BAR + ((NUM_BARS * 8 + 15) / 16) * 16;
+  static constexpr int SMEM_USED = OFF_MISC + 16;
+  static constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for manual 1024 B alignment
+
+  // Warp roles.
+  static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
+  static constexpr int LOAD_WARP = NUM_SOFTMAX_WARPS;
+  static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;
+  static constexpr int OBSERVER_WARP = NUM_SOFTMAX_WARPS + 2;  // profiler only
+  static constexpr int NUM_THREADS = 32 * (NUM_SOFTMAX_WARPS + 4);
+
+  static constexpr uint32_t IDESC_S = ptx::idesc_f16(128, BN, kBF16, false);
+  static constexpr uint32_t IDESC_PV = ptx::idesc_f16(128, D, kBF16, true);
+};
+
+// Lazy-rescale threshold in log2 units: O and the row sum are rescaled only
+// when the running max of a row grows by more than this; otherwise P is
+// computed against the stale max, so P <= 2^8 which f16, bf16 and the f32
+// accumulators all hold exactly enough.
+constexpr float RESCALE_THRESHOLD = 8.0f;
+
+struct WaitCtx {
+  volatile int* abort;  // CTA-local abort flag in shared memory
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+static __device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity, const WaitCtx& w,
+                                           int site) {
+  const unsigned long long t0 = ptx::globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((it & 31u) == 0) {
+      if (*w.abort) return false;
+      if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
+        *w.abort = 1;
+        if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + site);
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait for the completion of the mbarrier phase with parity `parity`.
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const WaitCtx& w,
+                                         int site) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  return wait_bar_slow(bar, parity, w, site);
+}
+
+template <bool PROFILE>
+struct Prof {
+  unsigned long long* buf;
+  __device__ __forceinline__ void stamp(int phase, int slot, int which) const {
+    if constexpr (PROFILE) {
+      if (buf != nullptr && slot < kProfSlots)
+        buf[(phase * kProfSlots + slot) * 2 + which] = clock64();
+    }
+  }
+};
+
+// ----------------------------------------------------------------------------
+// Producer: Q once, then the K/V sequence
+//   K_0 .. K_{NSBUF-1}, then for each j: V_j, K_{j+NSBUF}
+// which is exactly the order in which the MMA warp consumes ring slots.
+// ----------------------------------------------------------------------------
+template <class C, bool PROFILE>
+__device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const CUtensorMap* tmV,
+                          uint32_t sbase, int q_row0, int bh, const AttnParams& p,
+                          const WaitCtx& w, const Prof<PROFILE>& prof) {
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  const int n = p.num_kv_tiles;
+  const uint64_t pol_kv = ptx::l2_policy_evict_last();
+  const uint64_t pol_q = ptx::l2_policy_evict_first();
+
+  prof.stamp(kPhLoadQ, 0, 0);
+#pragma unroll
+  for (int i = 0; i < C::NQ; ++i) {
+    ptx::mbar_arrive_expect_tx(bar(C::BAR_Q + i), C::Q_TILE_BYTES);
+#pragma unroll
+    for (int d = 0; d < C::DBLK; ++d)
+      ptx::tma_load_3d_hint(sbase + C::OFF_Q + i * C::Q_TILE_BYTES + d * C::Q_BLK_BYTES, tmQ,
+                            bar(C::BAR_Q + i), d * 64, q_row0 + i * C::QROWS, bh, pol_q);
+  }
+  if (p.fault_mode == 1) return;  // test hook: K/V never arrive; consumers time out
+
+  int t = 0;          // ring item counter
+  int last_issued[C::STAGES];
+#pragma unroll
+  for (int s = 0; s < C::STAGES; ++s) last_issued[s] = -1;
+  bool ok = true;
+
+  auto produce = [&](bool is_k, int j) {
+    const int s = t % C::STAGES;
+    const int r = t / C::STAGES;
+    if (r > 0 && !wait_bar(bar(C::BAR_KV_EMPTY + s), (r - 1) & 1, w, kSiteKvEmpty)) {
+      ok = false;
+      return;
+    }
+    prof.stamp(is_k ? kPhLoadK : kPhLoadV, j, 0);
+    ptx::mbar_arrive_expect_tx(bar(C::BAR_KV_FULL + s), C::KV_TILE_BYTES);
+    const uint32_t dst = sbase + C::OFF_KV + s * C::KV_TILE_BYTES;
+#pragma unroll
+    for (int d = 0; d < C::DBLK; ++d)
+      ptx::tma_load_3d_hint(dst + d * C::KV_BLK_BYTES, is_k ? tmK : tmV, bar(C::BAR_KV_FULL + s),
+                            d * 64, j * C::BN, bh, pol_kv);
+    last_issued[s] = t;
+    ++t;
+  };
+
+  for (int jj = 0; jj < C::NSBUF && jj < n && ok; ++jj) produce(true, jj);
+  for (int j = 0; j < n && ok; ++j) {
+    produce(false, j);
+    if (ok && j + C::NSBUF < n) produce(true, j + C::NSBUF);
+  }
+  if (!ok) {
+    // Do not leave this CTA with bulk copies in flight: wait (bounded) for the
+    // most recent load issued into every slot to land.
+#pragma unroll
+    for (int s = 0; s < C::STAGES; ++s) {
+      if (last_issued[s] < 0) continue;
+      const int r = last_issued[s] / C::STAGES;
+      const unsigned long long t0 = ptx::globaltimer_ns();
+      while (!ptx::mbar_try_wait(bar(C::BAR_KV_FULL + s), r & 1)) {
+        if (ptx::globaltimer_ns() - t0 > w.timeout_ns) break;
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// MMA issuer (single thread)
+// ----------------------------------------------------------------------------
+template <class C, bool PROFILE>
+__device__ void mma_role(uint32_t tmem, uint32_t sbase, const AttnParams& p, const WaitCtx& w,
+                         const Prof<PROFILE>& prof) {
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  const int n = p.num_kv_tiles;
+  bool ok = true;
+
+  for (int i = 0; i < C::NQ && ok; ++i) ok = wait_bar(bar(C::BAR_Q + i), 0, w, kSiteQ);
+  if (ok) prof.stamp(kPhLoadQ, 0, 1);
+
+  int t = 0;
+  auto ring_wait = [&](int& stage) -> bool {
+    stage = t % C::STAGES;
+    const bool r = wait_bar(bar(C::BAR_KV_FULL + stage), (t / C::STAGES) & 1, w, kSiteKvFull);
+    ++t;
+    if (r) ptx::tc_fence_after();
+    return r;
+  };
+
+  // S_i(j) = Q_i K_j^T : D/16 MMAs of 128 x BN x 16.
+  auto issue_s = [&](int i, int j, int stage) {
+    const uint32_t d_tmem = tmem + (i * C::NSBUF + j % C::NSBUF) * C::BN;
+    const uint32_t qa = sbase + C::OFF_Q + i * C::Q_TILE_BYTES;
+    const uint32_t kb = sbase + C::OFF_KV + stage * C::KV_TILE_BYTES;
+#pragma unroll
+    for (int kk = 0; kk < C::D / 16; ++kk) {
+      const uint32_t koff = (kk & 3) * 32u;  // 16 elements = 32 B inside the 128 B row
+      const uint64_t ad = ptx::smem_desc_sw128(qa + (kk >> 2) * C::Q_BLK_BYTES + koff, 16, 1024);
+      const uint64_t bd = ptx::smem_desc_sw128(kb + (kk >> 2) * C::KV_BLK_BYTES + koff, 16, 1024);
+      ptx::mma_ss(d_tmem, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
+    }
+  };
+  // O_i += P_i(j) V_j : BN/16 MMAs of 128 x D x 16, A = P from TMEM.
+  auto issue_pv = [&](int i, int j, int stage) {
+    const uint32_t p_tmem = tmem + (i * C::NSBUF + j % C::NSBUF) * C::BN;
+    const uint32_t o_tmem = tmem + C::TMEM_O_COL + i * C::D;
+    const uint32_t vb = sbase + C::OFF_KV + stage * C::KV_TILE_BYTES;
+#pragma unroll
+    for (int kk = 0; kk < C::BN / 16; ++kk) {
+      const uint64_t bd = ptx::smem_desc_sw128(vb + kk * 2048u, C::KV_BLK_BYTES, 1024);
+      ptx::mma_ts(o_tmem, p_tmem + kk * 8, bd, C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+    }
+  };
+
+  // Prologue: S for the first NSBUF KV tiles.
+  for (int jj = 0; jj < C::NSBUF && jj < n && ok; ++jj) {
+    int sk;
+    if (!(ok = ring_wait(sk))) break;
+    for (int i = 0; i < C::NQ; ++i) {
+      if (i == 0) prof.stamp(kPhQK, jj, 0);
+      issue_s(i, jj, sk);
+      ptx::mma_commit(bar(C::BAR_S_FULL + i * C::NSBUF + jj % C::NSBUF));
+    }
+    ptx::mma_commit(bar(C::BAR_KV_EMPTY + sk));
+  }
+
+  for (int j = 0; j < n && ok; ++j) {
+    int sv;
+    if (!(ok = ring_wait(sv))) break;
+    const int jn = j + C::NSBUF;
+    int sk = -1;
+    for (int i = 0; i < C::NQ && ok; ++i) {
+      if (!(ok = wait_bar(bar(C::BAR_P_READY + i), j & 1, w, kSitePReady))) break;
+      ptx::tc_fence_after();
+      if (i == 0) prof.stamp(kPhPV, j, 0);
+      issue_pv(i, j, sv);
+      ptx::mma_commit(bar(C::BAR_O_DONE + i));
+      if (jn < n) {
+        if (sk < 0 && !(ok = ring_wait(sk))) break;
+        if (i == 0) prof.stamp(kPhQK, jn, 0);
+        issue_s(i, jn, sk);
+        ptx::mma_commit(bar(C::BAR_S_FULL + i * C::NSBUF + jn % C::NSBUF));
+      }
+    }
+    if (!ok) break;
+    ptx::mma_commit(bar(C::BAR_KV_EMPTY + sv));
+    if (sk >= 0) ptx::mma_commit(bar(C::BAR_KV_EMPTY + sk));
+  }
+
+  // Drain: every MMA this thread issued has completed before TMEM is freed.
+  ptx::mma_commit(bar(C::BAR_DRAIN));
+  const unsigned long long t0 = ptx::globaltimer_ns();
+  while (!ptx::mbar_try_wait(bar(C::BAR_DRAIN), 0)) {
+    if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
+      if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + kSiteDrain);
+      break;
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Softmax warpgroup for Q tile qi (128 threads; thread row = TMEM lane)
+// ----------------------------------------------------------------------------
+template <typename T, class C, bool PROFILE>
+__device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sgen,
+                             const CUtensorMap* tmO, int q_row0, int bh, const AttnParams& p,
+                             const WaitCtx& w, const Prof<PROFILE>& prof) {
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  const int wi = (threadIdx.x / 32) & 3;  // warp within the warpgroup = TMEM lane quarter
+  const int lane = threadIdx.x & 31;
+  const int row = wi * 32 + lane;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(wi * 32) << 16);
+  const uint32_t o_col = C::TMEM_O_COL + qi * C::D;
+  const int n = p.num_kv_tiles;
+  const float sl2 = p.scale_log2;
+  const bool rec = PROFILE && qi == 0 && wi == 0 && lane == 0;
+
+  float m_run = -INFINITY;  // running max (raw score units)
+  float l_run = 0.f;        // running row sum of P (relative to m_run)
+  bool ok = true;
+
+  for (int j = 0; j < n; ++j) {
+    const int buf = j % C::NSBUF;
+    const uint32_t s_col = (qi * C::NSBUF + buf) * C::BN;
+    ok = __all_sync(0xffffffffu,
+                    wait_bar(bar(C::BAR_S_FULL + qi * C::NSBUF + buf), (j / C::NSBUF) & 1, w,
+                             kSiteSFull));
+    if (!ok) break;
+    ptx::tc_fence_after();
+    if (rec) {
+      prof.stamp(kPhQK, j, 1);
+      prof.stamp(kPhSoftmax, j, 0);
+    }
+
+    const int lim = p.S - j * C::BN;  // valid key columns in this tile
+    float mx = -INFINITY;
+    constexpr int KEEP = C::BN <= 128;
+    constexpr int NCH = C::BN / 32;
+    uint32_t sreg[KEEP ? C::BN : 32];
+
+    if constexpr (KEEP) {
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        uint32_t(&r)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sreg[c * 32]);
+        ptx::tmem_ld32(lane_base + s_col + c * 32, r);
+      }
+      ptx::tmem_wait_ld();
+      ptx::reg_fence(sreg);
+      if (lim < C::BN) {
+#pragma unroll
+        for (int c = 0; c < C::BN; ++c)
+          if (c >= lim) sreg[c] = __float_as_uint(-INFINITY);
+      }
+#pragma unroll
+      for (int c = 0; c < C::BN; ++c) mx = fmaxf(mx, __uint_as_float(sreg[c]));
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < NCH; ++c) {
+        ptx::tmem_ld32(lane_base + s_col + c * 32, sreg);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(sreg);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float v = (c * 32 + e < lim) ? __uint_as_float(sreg[e]) : -INFINITY;
+          mx = fmaxf(mx, v);
+        }
+      }
+    }
+
+    // Lazy rescale decision.
+    float alpha = 1.f;
+    bool resc = false;
+    if (j == 0) {
+      m_run = mx;
+    } else if ((mx - m_run) * sl2 > RESCALE_THRESHOLD) {
+      alpha = ptx::ex2_approx((m_run - mx) * sl2);
+      m_run = mx;
+      resc = true;
+    }
+    if (__any_sync(0xffffffffu, resc)) {
+      // O holds the sum through PV(j-1); wait for that MMA, then scale in place.
+      ok = __all_sync(0xffffffffu, wait_bar(bar(C::BAR_O_DONE + qi), (j - 1) & 1, w, kSiteODone));
+      if (!ok) break;
+      ptx::tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < C::D / 32; ++c) {
+        uint32_t o[32];
+        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+        ptx::tmem_st32(lane_base + o_col + c * 32, o);
+      }
+    }
+
+    // P = exp2(s * scale_log2 - m * scale_log2), packed to T pairs over S.
+    const float neg = -m_run * sl2;
+    float sum = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      if constexpr (!KEEP) {
+        ptx::tmem_ld32(lane_base + s_col + c * 32, sreg);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(sreg);
+        if (lim < C::BN) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= lim) sreg[e] = __float_as_uint(-INFINITY);
+        }
+      }
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int c0 = (KEEP ? c * 32 : 0) + 2 * e;
+        const float p0 = ptx::ex2_approx(fmaf(__uint_as_float(sreg[c0]), sl2, neg));
+        const float p1 = ptx::ex2_approx(fmaf(__uint_as_float(sreg[c0 + 1]), sl2, neg));
+        sum += p0 + p1;
+        pk[e] = pack2<T>(p0, p1);
+      }
+      ptx::tmem_st16(lane_base + s_col + c * 16, pk);
+    }
+    ptx::tmem_wait_st();
+    ptx::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(bar(C::BAR_P_READY + qi));
+    if (rec) prof.stamp(kPhSoftmax, j, 1);
+    l_run = l_run * alpha + sum;
+  }
+
+  // Epilogue: wait for the last P V, normalise, stage in the Q slot, TMA store.
+  // Every warp of the group reaches both named barriers, also after a failed
+  // wait, so no warp can be left behind at a barrier; the abort flag (set by
+  // any timed-out wait before it returns) decides uniformly whether to store.
+  ptx::named_bar_sync(1 + qi, 128);
+  bool go = ok && (*w.abort == 0);
+  if (go) go = wait_bar(bar(C::BAR_O_DONE + qi), (n - 1) & 1, w, kSiteODone);
+  go = __all_sync(0xffffffffu, go);
+  const uint32_t stage_s = sbase + C::OFF_Q + qi * C::Q_TILE_BYTES;
+  if (go) {
+    ptx::tc_fence_after();
+    const float inv = 1.f / l_run;
+    uint8_t* stage_g = sgen + C::OFF_Q + qi * C::Q_TILE_BYTES;
+#pragma unroll 1
+    for (int c = 0; c < C::D / 32; ++c) {
+      uint32_t o[32];
+      ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+      ptx::tmem_wait_ld();
+      ptx::reg_fence(o);
+      const int dblk = (c * 32) / 64;
+      const int chunk0 = ((c * 32) % 64) / 8;  // first 16-byte chunk of these 32 columns
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 v;
+        v.x = pack2<T>(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
+        v.y = pack2<T>(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
+        v.z = pack2<T>(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
+        v.w = pack2<T>(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
+        const int chunk = (chunk0 + q) ^ (row & 7);
+        *reinterpret_cast<uint4*>(stage_g + dblk * C::Q_BLK_BYTES + row * 128 + chunk * 16) = v;
+      }
+    }
+    ptx::fence_proxy_async_smem();
+  }
+  ptx::named_bar_sync(1 + qi, 128);
+  if (wi == 0 && lane == 0 && *w.abort == 0) {
+#pragma unroll
+    for (int d = 0; d < C::DBLK; ++d)
+      ptx::tma_store_3d(tmO, stage_s + d * C::Q_BLK_BYTES, d * 64, q_row0 + qi * C::QROWS, bh);
+    ptx::tma_store_commit();
+    ptx::tma_store_wait_read0();
+  }
+}
+
+// Profiler observer: stamps the completion of each P V of Q tile 0.  It only
+// watches; a missed phase costs a stamp, never an error status.
+template <class C>
+__device__ void observer_role(uint32_t sbase, const AttnParams& p, const WaitCtx& w,
+                              const Prof<true>& prof) {
+  const uint32_t bar = sbase + C::OFF_BAR + 8u * (C::BAR_O_DONE + 0);
+  for (int j = 0; j < p.num_kv_tiles; ++j) {
+    const unsigned long long t0 = ptx::globaltimer_ns();
+    while (!ptx::mbar_try_wait(bar, j & 1)) {
+      if (*w.abort || ptx::globaltimer_ns() - t0 > w.timeout_ns) return;
+    }
+    prof.stamp(kPhPV, j, 1);
+  }
+}
+
+template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE>
+__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV,
+                    const __grid_constant__ CUtensorMap tmO, const AttnParams p) {
+  using C = AttnConfig<T, D, BN, NQ, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = ptx::smem_u32(smem_raw);
+  const uint32_t sbase = (raw_s + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - raw_s);
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int q_row0 = blockIdx.x * C::BM;
+  const int bh = blockIdx.y;
+
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + C::OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+    for (int i = 0; i < C::NQ; ++i) ptx::mbar_init(bar(C::BAR_Q + i), 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      ptx::mbar_init(bar(C::BAR_KV_FULL + s), 1);
+      ptx::mbar_init(bar(C::BAR_KV_EMPTY + s), 1);
+    }
+    for (int i = 0; i < C::NQ * C::NSBUF; ++i) ptx::mbar_init(bar(C::BAR_S_FULL + i), 1);
+    for (int i = 0; i < C::NQ; ++i) {
+      ptx::mbar_init(bar(C::BAR_P_READY + i), 4);
+      ptx::mbar_init(bar(C::BAR_O_DONE + i), 1);
+    }
+    ptx::mbar_init(bar(C::BAR_DRAIN), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == C::LOAD_WARP && lane == 0) {
+    ptx::tma_prefetch_desc(&tmQ);
+    ptx::tma_prefetch_desc(&tmK);
+    ptx::tma_prefetch_desc(&tmV);
+    ptx::tma_prefetch_desc(&tmO);
+  }
+  if (warp == C::MMA_WARP) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_slot), C::TMEM_ALLOC);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const WaitCtx w{abort_flag, p.status, p.timeout_ns};
+  const int cta_lin = blockIdx.y * gridDim.x + blockIdx.x;
+  Prof<PROFILE> prof{(PROFILE && cta_lin == p.prof_cta) ? p.prof : nullptr};
+
+  if (warp < C::NUM_SOFTMAX_WARPS) {
+    softmax_role<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, q_row0, bh, p, w, prof);
+  } else if (warp == C::LOAD_WARP) {
+    if (lane == 0) load_role<C, PROFILE>(&tmQ, &tmK, &tmV, sbase, q_row0, bh, p, w, prof);
+    __syncwarp();
+  } else if (warp == C::MMA_WARP) {
+    if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, p, w, prof);
+    __syncwarp();
+  } else if (warp == C::OBSERVER_WARP) {
+    if constexpr (PROFILE) {
+      if (lane == 0 && prof.buf != nullptr) observer_role<C>(sbase, p, w, prof);
+    }
+    __syncwarp();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == C::MMA_WARP) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, C::TMEM_ALLOC);
+  }
+}
+
+}  // namespace attnprof

@@ -1,0 +1,407 @@
+#!/usr/bin/env python3
+"""Benchmark of the attention forward engine (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5]
+                    [--impl ours|reference]
+
+A step is one attention forward over one batch of synthetic inputs (seeded
+N(0, sigma^2)).  Default workload C2 = B=1, H=16, S=4096, D=128 fp16 per GPU,
+the configuration the north-star metric is quoted on; with N GPUs the global
+batch is B=N and each GPU owns its (batch, head) units -- no collective on the
+data path (weak scaling).  C4/C5 are the strong-scaling sharded shapes.
+
+Metric: attn fwd TFLOP/s = 4*B*H*S^2*D / t, whole job, t = max over ranks of
+the device time (CUDA events) of exactly K steps.  `e2e` repeats the metric
+through the public API with pinned host buffers and the H2D/D2H copies inside
+the timed region.  `cpu_baseline` times the reference's own host attention
+(oracle/_ref, the reference's verify_attn compiled from its sources) on this
+host.  `--impl reference` is the reference arm: the reference's CPU attention
+algorithm (oracle port, bit-identical to the reference's output on the golden
+fixtures) on all host threads, one bounded sample of the workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # name: (B, H, S, D, dtype, sigma, scaling)
+    "c2": dict(B=1, H=16, S=4096, D=128, dtype="f16", sigma=1.0, scaling="weak"),
+    "c3": dict(B=1, H=16, S=4096, D=64, dtype="f16", sigma=1.0, scaling="weak"),
+    "c4": dict(B=8, H=32, S=8192, D=128, dtype="bf16", sigma=1.0, scaling="strong"),
+    "c5": dict(B=1, H=64, S=32768, D=128, dtype="f16", sigma=0.5, scaling="strong"),
+}
+# Published reference figures for the same metric and shape (Hopper, 114 SMs;
+# README.md:333-337 for C2, README.md:265-270 for C3).  None elsewhere.
+PUBLISHED = {"c2": 309.022, "c3": 296.931}
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "attn fwd TFLOP/s (4*B*H*S^2*D/t)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--bm", type=int, default=256)
+    ap.add_argument("--bn", type=int, default=128)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--preroll-s", type=float, default=0.5,
+                    help="untimed back-to-back launches before timing (clock warm-up)")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+def flops(units, S, D):
+    return 4.0 * units * float(S) * S * D
+
+
+def config_of(wl, args, n):
+    w = WORKLOADS[wl]
+    if w["scaling"] == "weak":
+        B = w["B"] * n
+        desc = (f"{wl.upper()}: per GPU B={w['B']},H={w['H']},S={w['S']},D={w['D']} {w['dtype']}; "
+                f"global B={B} sharded by (batch, head), no collective")
+    else:
+        B = w["B"]
+        desc = (f"{wl.upper()}: B={w['B']},H={w['H']},S={w['S']},D={w['D']} {w['dtype']} "
+                f"sharded by (batch, head) over {n} GPU(s), no collective")
+    return {"workload": desc, "B": B, "H": w["H"], "S": w["S"], "D": w["D"],
+            "BM": args.bm, "BN": args.bn, "inputs": f"N(0,{w['sigma']}^2) seeded {args.seed}",
+            "accumulate": "fp32", "causal": False}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own host attention (oracle/_ref)
+# ---------------------------------------------------------------------------
+def cpu_baseline_reference(wl):
+    from oracle import oracle
+    exe = oracle.ref_binary()
+    cfg = {"c2": "c2head", "c3": "c3head"}.get(wl, "c2head")
+    threads = max(1, min(os.cpu_count() or 1, 16))
+    if not exe.exists():
+        return None
+    r = subprocess.run([str(exe), "time", cfg, str(threads)], capture_output=True, text=True,
+                       timeout=600)
+    line = [ln for ln in r.stderr.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not line:
+        return None
+    d = json.loads(line[-1])
+    D = 128 if cfg == "c2head" else 64
+    return {"value": d["tflops"], "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+            "sample": (f"{d['heads']} heads of 1x1x4096x{D} fp16 (one C2/C3 head per thread), "
+                       f"the reference's verify_attn host oracle (tuning/utils.cuh:139-198) "
+                       f"compiled from its sources; {d['seconds']:.2f} s wall")}
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    import torch
+    from oracle import oracle
+    w = WORKLOADS[args.workload]
+    n = args.gpus
+    cfg = config_of(args.workload, args, n)
+    B, H, S, D = cfg["B"], w["H"], w["S"], w["D"]
+    dt = 0 if w["dtype"] == "f16" else 1
+    tdt = torch.float16 if dt == 0 else torch.bfloat16
+    # Inputs of one C-unit group (the rows sampled per step come from them).
+    Bs = min(B, 1)
+    g = torch.Generator().manual_seed(args.seed)
+    q, k, v = ((torch.randn(Bs, H, S, D, generator=g) * w["sigma"]).to(tdt)
+               .view(torch.int16).numpy().view(np.uint16) for _ in range(3))
+    threads = oracle.max_threads()
+    rows_per_step = 1024
+    rng = np.random.default_rng(args.seed)
+
+    def step(i):
+        rows = rng.choice(Bs * H * S, size=rows_per_step, replace=False).astype(np.int64)
+        oracle.attention_rows(q, k, v, rows, bn_tile=args.bn, dtype=dt, nthreads=threads)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    sec = time.perf_counter() - t0
+    f = 4.0 * rows_per_step * S * D * args.steps
+    val = f / sec / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": n,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec / args.steps * 1e3,
+        "higher_is_better": True, "scaling": w["scaling"], "vs_baseline": None,
+        "dtype": w["dtype"], "data": "synthetic", "config": cfg,
+        "cpu_baseline": {
+            "value": val, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": (f"{rows_per_step} query rows of the {args.workload.upper()} workload per "
+                       f"step ({S} keys, D={D}), the reference's host attention algorithm "
+                       "(oracle/attn_oracle.c, bit-identical to the reference's verify_attn on "
+                       "tests/golden) on all host threads")},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    import attnprofile_b200 as ap
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n = world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    w = WORKLOADS[args.workload]
+    cfg = config_of(args.workload, args, n)
+    S, D, H = w["S"], w["D"], w["H"]
+    tdt = torch.float16 if w["dtype"] == "f16" else torch.bfloat16
+    units_total = cfg["B"] * H
+    u0, u1 = ap.shard_range(units_total, n, rank)
+    units = u1 - u0
+    elt = 2
+    set_bytes = 4 * units * S * D * elt
+    n_sets = 1 if set_bytes >= L2_BYTES else min(4, max(2, math.ceil(2 * L2_BYTES / set_bytes)))
+
+    # Seeded inputs, generated per global unit so a unit's data does not depend
+    # on the number of GPUs.
+    def gen_set(s):
+        Q = torch.empty(1, units, S, D, dtype=tdt, device=dev)
+        K, V = torch.empty_like(Q), torch.empty_like(Q)
+        for i, u in enumerate(range(u0, u1)):
+            g = torch.Generator(device=dev).manual_seed(args.seed * 1000003 + s * 7919 + u)
+            for t in (Q, K, V):
+                t[0, i].copy_((torch.randn(S, D, generator=g, device=dev) * w["sigma"]).to(tdt))
+        return Q, K, V, torch.empty_like(Q)
+
+    sets = [gen_set(s) for s in range(n_sets)]
+    torch.cuda.synchronize()
+
+    def launch(i):
+        Q, K, V, O = sets[i % n_sets]
+        ap.attn(Q, K, V, O, BM=args.bm, BN=args.bn)
+
+    for i in range(max(args.warmup, 3)):
+        launch(i)
+    torch.cuda.synchronize()
+    rc, site = ap.get_status(local)
+    if rc != 0:
+        raise SystemExit(f"device status after warm-up: {rc} site {site:#x}")
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_end = time.perf_counter() + args.preroll_s
+    i = 0
+    while time.perf_counter() < t_end:
+        launch(i)
+        i += 1
+        if i % 64 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for i in range(args.steps):
+        launch(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    rc, site = ap.get_status(local)
+    if rc != 0:
+        raise SystemExit(f"device status after timing: {rc} site {site:#x}")
+
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    total_flops = flops(units_total, S, D) * args.steps
+    value = total_flops / (ms_max * 1e-3) / 1e12
+
+    # roofline of the (only) kernel: algorithmic FLOPs per launch / mean launch time
+    per_launch_ms = ms / args.steps
+    achieved = flops(units, S, D) / (per_launch_ms * 1e-3) / 1e12
+    burst, sustained, kind = peaks()
+    peak = sustained if ms > 1000.0 else burst
+    traffic = None
+    tf = ROOT / "profiles" / "ncu_traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get(args.workload, {}).get(
+                f"bm{args.bm}_bn{args.bn}")
+        except Exception:
+            traffic = None
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        Q, K, V, O = sets[0]
+        hq, hk, hv = (x.cpu().pin_memory() for x in (Q, K, V))
+        ho = torch.empty(O.shape, dtype=tdt).pin_memory()
+        steps_e = max(1, min(args.steps, 20))
+        for _ in range(2):
+            Q.copy_(hq, non_blocking=True); K.copy_(hk, non_blocking=True)
+            V.copy_(hv, non_blocking=True)
+            ap.attn(Q, K, V, O, BM=args.bm, BN=args.bn)
+            ho.copy_(O, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps_e):
+            Q.copy_(hq, non_blocking=True); K.copy_(hk, non_blocking=True)
+            V.copy_(hv, non_blocking=True)
+            ap.attn(Q, K, V, O, BM=args.bm, BN=args.bn)
+            ho.copy_(O, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": flops(units_total, S, D) * steps_e / (float(te.item()) * 1e-3) / 1e12,
+               "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * hq.numel() * elt,
+               "d2h_bytes_per_step": ho.numel() * elt, "steps": steps_e,
+               "api": "attnprofile_b200.attn -> attn_fwd (C ABI)"}
+
+    launches = torch.tensor([args.steps], dtype=torch.int64, device=dev)
+    if world > 1:
+        dist.all_reduce(launches)
+
+    cpu = None
+    if rank == 0 and n == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_reference(args.workload)
+
+    if rank == 0:
+        cfg["l2"] = (f"{n_sets} rotating input sets ({n_sets * set_bytes / 2**20:.0f} MiB) vs "
+                     f"126 MiB L2" if n_sets > 1 else "inputs larger than the 126 MiB L2")
+        pub = PUBLISHED.get(args.workload)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": n,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": w["scaling"],
+            "vs_baseline": (value / pub) if pub else None,
+            "dtype": w["dtype"], "data": "synthetic", "config": cfg,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{kind} {'sustained' if peak == sustained else 'burst'}"
+                                        " bf16 cuBLAS (MEASURED_PEAKS.json)",
+                         "kernel": "attn_fwd_kernel"},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches.item()),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,143 @@
+/*
+ * attnprof.h -- C ABI of the B200 (sm_100a) attention forward engine.
+ *
+ * Non-causal attention O = softmax(Q K^T / sqrt(D)) V over tensors laid out
+ * row-major as [B, H, rows, D] (rows = S unless stated), f16 or bf16 in and
+ * out, fp32 accumulation.  All pointers are device pointers of the current
+ * CUDA device unless stated.  Calls are asynchronous on the given stream
+ * (NULL = legacy default stream) unless stated; the functions never
+ * synchronise except where the comment says so.
+ *
+ * The reference (Xiebaokang/AttnProfile) exposes this path only as C++
+ * templates compiled per configuration:
+ *   runAttn<B,H,S,D,BM,BN,NUM_SMEM,PRODUCER_REG_DEALLOC,CONSUMER_REG_ALLOC,
+ *           P_SMEM_K_TILES,KERNEL_IDX,NUM_THREADS>(fp16* Q, fp16* K,
+ *           fp16* V, fp16* O)                      tuning/attn_test.cu:1665-1691
+ * passed around as AttnRunner = void(*)(fp16*,fp16*,fp16*,fp16*)
+ *                                                 tuning/utils.cuh:71
+ * The entry points below are what a foreign-function binding of that path
+ * binds: shape and tile at run time, an explicit stream, and error codes in
+ * place of the reference's cudaCheck -> exit(1) (tuning/tools.cuh:14-21).
+ */
+#ifndef ATTNPROF_H
+#define ATTNPROF_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ATTN_DTYPE_F16 0
+#define ATTN_DTYPE_BF16 1
+
+/* Return codes (0 = success, negative = error). */
+#define ATTN_OK 0
+#define ATTN_ERR_INVALID_ARG -1    /* null pointer, non-positive size, rows < S, ... */
+#define ATTN_ERR_UNSUPPORTED -2    /* (dtype, D, BM, BN) combination not built      */
+#define ATTN_ERR_MISALIGNED -3     /* a tensor base is not 16-byte aligned          */
+#define ATTN_ERR_CUDA -4           /* CUDA runtime error (no device, launch error)  */
+#define ATTN_ERR_TENSOR_MAP -5     /* cuTensorMapEncodeTiled rejected the layout    */
+#define ATTN_ERR_DEVICE_TIMEOUT -6 /* a bounded in-kernel wait expired              */
+#define ATTN_ERR_RESOURCE -7       /* shared memory / TMEM request over the limit   */
+#define ATTN_ERR_SHARD -8          /* multi-GPU partition error                     */
+
+/*
+ * attn_fwd -- one attention forward over contiguous [B, H, S, D] tensors.
+ * BM in {128, 256} query rows per CTA; BN in {32, 64, 128, 256} keys per KV
+ * tile (BM = 256 with BN = 256 does not fit tensor memory: UNSUPPORTED).
+ * D in {64, 128}.  B*H <= 65535.  Asynchronous; returns launch errors only
+ * (device-side timeouts are reported by attn_get_status).
+ * Replaces: runAttn<...>(Q, K, V, O)            tuning/attn_test.cu:1665-1691
+ *           (BM, BN as run-time values instead of template parameters).
+ */
+int attn_fwd(const void* Q, const void* K, const void* V, void* O, int B, int H, int S, int D,
+             int dtype, int BM, int BN, void* stream);
+
+/*
+ * attn_fwd_padded -- the reference's padded layout: Q and O are
+ * [B, H, SQO, D], K and V are [B, H, SKV, D], with SQO >= S and SKV >= S
+ * (the reference allocates SQO = ceil(S/BM)*BM, SKV = ceil(S/BN)*BN,
+ * tuning/attn_test.cu:1590-1595, tuning/utils.cuh:86-87).  Rows >= S are
+ * neither read nor written.
+ * Replaces: runAttnWS2StageBaselineKernel / ...SmemP... / ...ForNSmemP...
+ *           launchers                         tuning/attn_test.cu:1583-1663
+ */
+int attn_fwd_padded(const void* Q, const void* K, const void* V, void* O, int B, int H, int S,
+                    int D, int SQO, int SKV, int dtype, int BM, int BN, void* stream);
+
+/*
+ * attn_fwd_profiled -- attn_fwd with the per-phase cycle profiler compiled in
+ * (f16 and bf16).  CTA number profile_cta (blockIdx.y * gridDim.x + blockIdx.x)
+ * writes clock64 begin/end stamps for the phases LoadQ, LoadK, LoadV, GEMM-QK,
+ * SOFTMAX, GEMM-PV of its first 32 KV iterations into dev_profile_buf, laid
+ * out as u64 [6][32][2] (see attn_profile_layout).  The caller zeroes the
+ * buffer before the launch; unstamped slots stay 0.
+ * Replaces: the clock64 profiler of attn.cu (ProfileResult attn.cu:5-22,
+ *           stamps attn.cu:133-444, run_one_case attn.cu:1400-1494).
+ */
+int attn_fwd_profiled(const void* Q, const void* K, const void* V, void* O, int B, int H, int S,
+                      int D, int dtype, int BM, int BN, void* stream,
+                      unsigned long long* dev_profile_buf, int profile_cta);
+
+/* Profile buffer geometry: *phases = 6, *slots = 32 (u64 pairs). */
+int attn_profile_layout(int* phases, int* slots);
+
+/*
+ * attn_fwd_sharded -- (batch, head) sharding over n_dev GPUs of this process,
+ * no collective.  Units u = b*H + h are split as [g*U/n, (g+1)*U/n) for
+ * GPU g (see attn_shard_range); Q[g], K[g], V[g], O[g] are device pointers on
+ * devices[g] holding that GPU's units contiguously ([units_g, S, D]).
+ * Launches on every device, then synchronises them all (this call blocks).
+ * ms_per_device (optional, host array of n_dev) receives each device's
+ * kernel time in milliseconds from CUDA events.
+ * No counterpart in the reference (single-GPU only); this is the (b,h)
+ * partition the benchmark configurations C4/C5 run on 1/2/4/8 GPUs.
+ */
+int attn_fwd_sharded(int n_dev, const int* devices, const void* const* Q, const void* const* K,
+                     const void* const* V, void* const* O, int B, int H, int S, int D, int dtype,
+                     int BM, int BN, float* ms_per_device);
+
+/* The partition rule used by attn_fwd_sharded: units [*begin, *end) of GPU g. */
+int attn_shard_range(int units, int n_dev, int g, int* begin, int* end);
+
+/*
+ * attn_get_status -- synchronise `device` and read the device status word
+ * that bounded in-kernel waits set on expiry.  Returns ATTN_OK or
+ * ATTN_ERR_DEVICE_TIMEOUT (*site, if non-NULL, receives the raw code);
+ * reset != 0 clears the word.  Blocking.
+ * Replaces: the reference's unbounded mbarrier spin (tuning/tools.cuh:870-885),
+ * which has no error path.
+ */
+int attn_get_status(int device, int reset, int* site);
+
+/* Bounded-wait limit for kernels launched after this call (default 2 s). */
+void attn_set_timeout_ns(unsigned long long ns);
+
+/*
+ * attn_query_config -- launch geometry of a (D, BM, BN, dtype) variant:
+ * threads per CTA, dynamic shared memory bytes, TMEM columns allocated and
+ * K/V ring depth.  Returns ATTN_ERR_UNSUPPORTED for combinations not built.
+ * Replaces: the reference's resource model (tuning/solver.py:14-95), which
+ * the tuning harness uses to filter configurations.
+ */
+int attn_query_config(int D, int BM, int BN, int dtype, int* num_threads, int* smem_bytes,
+                      int* tmem_cols, int* stages);
+
+/* Human-readable text for a return code.  Never NULL. */
+const char* attn_error_string(int code);
+
+/*
+ * attn_debug_fault -- test hook for the failure path: mode 1 makes the next
+ * launches' producer warp load Q but never K/V, so every consumer's bounded
+ * wait expires and the kernel returns with ATTN_ERR_DEVICE_TIMEOUT in the
+ * status word (no fault, no trap, no hang).  mode 0 restores normal runs.
+ */
+int attn_debug_fault(int mode);
+
+/* ABI version (major*100 + minor). */
+int attn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATTNPROF_H */

@@ -1,0 +1,256 @@
+/*
+ * attn_oracle.c -- CPU restatement of the reference's host-side attention.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA
+ * engine; only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
+ * leg load it.  The engine never calls it and has no CPU fallback.
+ *
+ * It follows the oracle inside verify_attn (tuning/utils.cuh:139-198) step by
+ * step, in the same floating-point order:
+ *   attn_scale = sqrtf(1.0f / D) * 1.44269504f                 utils.cuh:139
+ *   per (b, h, query row):                                     utils.cuh:143-196
+ *     row_max = -FLT_MAX, row_sum = 0, row_acc[D] = 0
+ *     for each key tile [iw, min(iw + BN_TILE, S)):            utils.cuh:152
+ *       score = sum_d q[d] * k[d]   (fp32, d ascending)        utils.cuh:156-162
+ *       tile_max = max(score)                                  utils.cuh:163
+ *       new_max = fmaxf(row_max, tile_max)                     utils.cuh:166
+ *       old_scale = row_max == -FLT_MAX ? 0                    utils.cuh:167-169
+ *                   : exp2f(row_max*scale - new_max*scale)
+ *       row_acc *= old_scale                                   utils.cuh:171-173
+ *       prob = exp2f(score*scale - new_max*scale)              utils.cuh:177
+ *       tile_sum += prob          (unrounded)                  utils.cuh:178
+ *       row_acc[d] += half(prob) * v[d]   (P rounded to the    utils.cuh:181-184
+ *                                          storage type first)
+ *       row_sum = row_sum * old_scale + tile_sum               utils.cuh:187
+ *     O = round(row_acc[d] * (1.0f / row_sum))                 utils.cuh:191-194
+ * Build with -ffp-contract=off so no multiply-add is fused (the reference's
+ * host code is plain x86-64 SSE arithmetic).  For bf16 the same steps run with
+ * bf16 in place of fp16 (the reference has fp16 only).
+ *
+ * Parity pin: tests/golden holds outputs of the reference's own verify_attn
+ * (compiled from its sources under a host shim, oracle/ref_shim.cu); this
+ * restatement reproduces them bit for bit.
+ */
+#include <float.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ---- storage-type conversions (IEEE round-to-nearest-even) ---- */
+
+uint16_t oracle_f32_to_f16(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u;
+  const uint32_t ax = x & 0x7FFFFFFFu;
+  if (ax >= 0x7F800000u) return (uint16_t)(sign | (ax > 0x7F800000u ? 0x7E00u : 0x7C00u));
+  if (ax >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u); /* >= 65520 rounds to inf */
+  if (ax < 0x38800000u) {                                      /* below 2^-14: subnormal */
+    float a;
+    memcpy(&a, &ax, 4);
+    const float m = rintf(a * 16777216.0f); /* units of 2^-24, ties to even */
+    return (uint16_t)(sign | (uint32_t)m);
+  }
+  const uint32_t mant = ax & 0x7FFFFFu;
+  const uint32_t e = (ax >> 23) - 127u + 15u;
+  uint32_t h = (e << 10) | (mant >> 13);
+  const uint32_t rem = mant & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+  return (uint16_t)(sign | h);
+}
+
+float oracle_f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t e = (h >> 10) & 0x1Fu;
+  const uint32_t m = h & 0x3FFu;
+  uint32_t x;
+  if (e == 0) {
+    if (m == 0) {
+      x = sign;
+    } else { /* subnormal: m * 2^-24 */
+      float f = (float)m * (1.0f / 16777216.0f);
+      memcpy(&x, &f, 4);
+      x |= sign;
+    }
+  } else if (e == 31) {
+    x = sign | 0x7F800000u | (m << 13);
+  } else {
+    x = sign | ((e - 15u + 127u) << 23) | (m << 13);
+  }
+  float f;
+  memcpy(&f, &x, 4);
+  return f;
+}
+
+uint16_t oracle_f32_to_bf16(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  if ((x & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((x >> 16) | 0x40u);
+  x += 0x7FFFu + ((x >> 16) & 1u);
+  return (uint16_t)(x >> 16);
+}
+
+float oracle_bf16_to_f32(uint16_t b) {
+  const uint32_t x = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &x, 4);
+  return f;
+}
+
+static inline float to_f32(uint16_t v, int bf16) {
+  return bf16 ? oracle_bf16_to_f32(v) : oracle_f16_to_f32(v);
+}
+static inline uint16_t from_f32(float v, int bf16) {
+  return bf16 ? oracle_f32_to_bf16(v) : oracle_f32_to_f16(v);
+}
+
+/* One query row.  q: D values (storage type); K, V: this head's [skv][D];
+ * out: D values (storage type).  scores: scratch of S floats, acc: D floats. */
+static void attn_row(const uint16_t* q, const uint16_t* Kh, const uint16_t* Vh, uint16_t* out,
+                     int S, int D, int bn_tile, int bf16, float* scores, float* acc,
+                     float* qf) {
+  const float attn_scale = sqrtf(1.0f / (float)D) * 1.44269504f;
+  for (int d = 0; d < D; ++d) {
+    acc[d] = 0.0f;
+    qf[d] = to_f32(q[d], bf16);
+  }
+  float row_max = -FLT_MAX;
+  float row_sum = 0.0f;
+  for (int iw = 0; iw < S; iw += bn_tile) {
+    const int tile_end = iw + bn_tile < S ? iw + bn_tile : S;
+    float tile_max = -FLT_MAX;
+    for (int s2 = iw; s2 < tile_end; ++s2) {
+      const uint16_t* k = Kh + (size_t)s2 * D;
+      float score = 0.0f;
+      for (int d = 0; d < D; ++d) score += qf[d] * to_f32(k[d], bf16);
+      scores[s2] = score;
+      tile_max = fmaxf(tile_max, score);
+    }
+    const float new_max = fmaxf(row_max, tile_max);
+    const float old_scale =
+        (row_max == -FLT_MAX) ? 0.0f : exp2f(row_max * attn_scale - new_max * attn_scale);
+    for (int d = 0; d < D; ++d) acc[d] *= old_scale;
+    float tile_sum = 0.0f;
+    for (int s2 = iw; s2 < tile_end; ++s2) {
+      const float prob = exp2f(scores[s2] * attn_scale - new_max * attn_scale);
+      tile_sum += prob;
+      const float prob_for_pv = to_f32(from_f32(prob, bf16), bf16);
+      const uint16_t* v = Vh + (size_t)s2 * D;
+      for (int d = 0; d < D; ++d) acc[d] += prob_for_pv * to_f32(v[d], bf16);
+    }
+    row_sum = row_sum * old_scale + tile_sum;
+    row_max = new_max;
+  }
+  const float inv_sum = 1.0f / row_sum;
+  for (int d = 0; d < D; ++d) out[d] = from_f32(acc[d] * inv_sum, bf16);
+}
+
+static int check_args(int B, int H, int S, int D, long sqo, long skv, int bn_tile, int dtype) {
+  if (B < 0 || H < 0 || S < 0 || D <= 0 || bn_tile <= 0) return -1;
+  if (sqo < S || skv < S) return -1;
+  if (dtype != 0 && dtype != 1) return -2;
+  return 0;
+}
+
+/*
+ * Full attention.  Q/O: [B, H, sqo, D]; K/V: [B, H, skv, D] (storage type
+ * dtype: 0 = f16, 1 = bf16).  Rows >= S of O are left untouched.
+ * nthreads <= 0 uses every OpenMP thread; 1 runs single-threaded as the
+ * reference does.  Returns 0, or -1 / -2 on bad arguments, -3 on no memory.
+ */
+int oracle_attn(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int B,
+                int H, int S, int D, long sqo, long skv, int bn_tile, int dtype, int nthreads) {
+  const int rc = check_args(B, H, S, D, sqo, skv, bn_tile, dtype);
+  if (rc) return rc;
+  const long total = (long)B * H * S;
+  int err = 0;
+#ifdef _OPENMP
+  const int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel num_threads(nt)
+#endif
+  {
+    float* scores = (float*)malloc(sizeof(float) * (size_t)(S > 0 ? S : 1));
+    float* acc = (float*)malloc(sizeof(float) * (size_t)D);
+    float* qf = (float*)malloc(sizeof(float) * (size_t)D);
+    if (!scores || !acc || !qf) {
+#ifdef _OPENMP
+#pragma omp atomic write
+#endif
+      err = -3;
+    } else {
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 16)
+#endif
+      for (long r = 0; r < total; ++r) {
+        const long u = r / S;
+        const long s = r % S;
+        const uint16_t* Kh = K + (size_t)u * skv * D;
+        const uint16_t* Vh = V + (size_t)u * skv * D;
+        attn_row(Q + ((size_t)u * sqo + s) * D, Kh, Vh, O + ((size_t)u * sqo + s) * D, S, D,
+                 bn_tile, dtype, scores, acc, qf);
+      }
+    }
+    free(scores);
+    free(acc);
+    free(qf);
+  }
+  (void)nthreads;
+  return err;
+}
+
+/*
+ * Selected query rows only (for shapes whose full oracle would take hours):
+ * rows[i] = u * S + s with u = b * H + h; out is [n][D].
+ */
+int oracle_attn_rows(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* out,
+                     const int64_t* rows, long n, int B, int H, int S, int D, long sqo, long skv,
+                     int bn_tile, int dtype, int nthreads) {
+  const int rc = check_args(B, H, S, D, sqo, skv, bn_tile, dtype);
+  if (rc) return rc;
+  for (long i = 0; i < n; ++i)
+    if (rows[i] < 0 || rows[i] >= (int64_t)B * H * S) return -1;
+  int err = 0;
+#ifdef _OPENMP
+  const int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel num_threads(nt)
+#endif
+  {
+    float* scores = (float*)malloc(sizeof(float) * (size_t)(S > 0 ? S : 1));
+    float* acc = (float*)malloc(sizeof(float) * (size_t)D);
+    float* qf = (float*)malloc(sizeof(float) * (size_t)D);
+    if (!scores || !acc || !qf) {
+#ifdef _OPENMP
+#pragma omp atomic write
+#endif
+      err = -3;
+    } else {
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 4)
+#endif
+      for (long i = 0; i < n; ++i) {
+        const long u = (long)(rows[i] / S);
+        const long s = (long)(rows[i] % S);
+        attn_row(Q + ((size_t)u * sqo + s) * D, K + (size_t)u * skv * D, V + (size_t)u * skv * D,
+                 out + (size_t)i * D, S, D, bn_tile, dtype, scores, acc, qf);
+      }
+    }
+    free(scores);
+    free(acc);
+    free(qf);
+  }
+  (void)nthreads;
+  return err;
+}
+
+int oracle_max_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}

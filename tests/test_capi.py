@@ -1,0 +1,107 @@
+"""C-ABI library: loads without a GPU, exports every declared symbol, and
+validates arguments on the host (no kernel is launched here)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "attnprof.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(attn_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for must in ("attn_fwd", "attn_fwd_padded", "attn_fwd_profiled", "attn_fwd_sharded",
+                 "attn_error_string", "attn_get_status", "attn_query_config"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(engine):
+    L = engine.lib()
+    missing = [n for n in declared_functions() if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_library_has_no_libcuda_link_dependency(engine):
+    import subprocess
+    out = subprocess.run(["ldd", str(engine.LIB_PATH)], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in out
+
+
+def test_error_strings(engine):
+    L = engine.lib()
+    for code in list(engine.ERR.values()) + [-99]:
+        s = L.attn_error_string(code)
+        assert s and len(s) > 1
+
+
+@pytest.mark.parametrize("units,n", [(16, 1), (16, 3), (256, 8), (64, 8), (5, 8), (0, 4)])
+def test_shard_range_partitions_units(engine, units, n):
+    spans = [engine.shard_range(units, n, g) for g in range(n)]
+    assert spans[0][0] == 0 and spans[-1][1] == units
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 == b0
+    sizes = [e - b for b, e in spans]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_shard_range_rejects_bad_rank(engine):
+    b, e = ctypes.c_int(), ctypes.c_int()
+    assert engine.lib().attn_shard_range(16, 4, 4, ctypes.byref(b), ctypes.byref(e)) == -8
+
+
+@pytest.mark.parametrize("bm,bn", [(128, 32), (128, 64), (128, 128), (128, 256), (256, 32),
+                                   (256, 64), (256, 128)])
+@pytest.mark.parametrize("d", [64, 128])
+def test_query_config_fits_b200(engine, bm, bn, d):
+    for dt in (0, 1):
+        c = engine.query_config(d, bm, bn, dt)
+        assert c["smem_bytes"] <= 232448
+        assert c["tmem_cols"] in (32, 64, 128, 256, 512)
+        assert c["stages"] >= 2
+        assert c["num_threads"] == 32 * (4 * (bm // 128) + 4)
+
+
+@pytest.mark.parametrize("d,bm,bn", [(128, 256, 256), (96, 128, 128), (128, 64, 128),
+                                     (128, 128, 48)])
+def test_query_config_rejects_unbuilt(engine, d, bm, bn):
+    vals = [ctypes.c_int() for _ in range(4)]
+    rc = engine.lib().attn_query_config(d, bm, bn, 0, *[ctypes.byref(v) for v in vals])
+    assert rc == engine.ERR["UNSUPPORTED"]
+
+
+def test_host_validation_without_gpu(engine):
+    L = engine.lib()
+    good = 0x10000
+    # empty problem: nothing to do, success
+    assert L.attn_fwd(good, good, good, good, 0, 16, 4096, 128, 0, 128, 128, None) == 0
+    assert L.attn_fwd(good, good, good, good, 1, 1, 0, 128, 0, 128, 128, None) == 0
+    # bad arguments
+    assert L.attn_fwd(good, good, good, good, 1, 1, -1, 128, 0, 128, 128, None) == -1
+    assert L.attn_fwd(None, good, good, good, 1, 1, 16, 128, 0, 128, 128, None) == -1
+    assert L.attn_fwd(good + 2, good, good, good, 1, 1, 16, 128, 0, 128, 128, None) == -3
+    assert L.attn_fwd(good, good, good, good, 1, 1, 16, 96, 0, 128, 128, None) == -2
+    assert L.attn_fwd(good, good, good, good, 1, 1, 16, 128, 7, 128, 128, None) == -2
+    assert L.attn_fwd(good, good, good, good, 1, 65536, 16, 128, 0, 128, 128, None) == -1
+    # padded rows fewer than S
+    assert L.attn_fwd_padded(good, good, good, good, 1, 1, 64, 128, 32, 64, 0, 128, 128,
+                             None) == -1
+    # profiled call needs a buffer
+    assert L.attn_fwd_profiled(good, good, good, good, 1, 1, 64, 128, 0, 128, 128, None,
+                               None, 0) == -1
+
+
+def test_no_cpu_fallback_without_gpu(engine):
+    """With no usable GPU a valid call fails loudly; it never computes on the host."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    good = 0x10000
+    rc = engine.lib().attn_fwd(good, good, good, good, 1, 1, 64, 128, 0, 128, 128, None)
+    assert rc == engine.ERR["CUDA"]

@@ -1,0 +1,151 @@
+"""GPU parity of the sm_100a kernel against the CPU oracle (calls go through the
+C ABI via attnprofile_b200).
+
+Tolerance (from the task's north star, fp16 and bf16 alike):
+    max |O_gpu - O_oracle| <= 2e-3   and   mean |O_gpu - O_oracle| <= 2e-4
+compared in fp32 after decoding both 16-bit outputs.  The oracle runs with the
+same key tile (bn_tile = BN) as the kernel.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-3
+MEAN_ABS = 2e-4
+TILES = [(128, 32), (128, 64), (128, 128), (128, 256), (256, 32), (256, 64), (256, 128)]
+GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+
+
+def _torch():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def make_inputs(B, H, S, D, dtype, seed=0, sigma=1.0):
+    torch = _torch()
+    g = torch.Generator().manual_seed(seed)
+    t = [(torch.randn(B, H, S, D, generator=g) * sigma).to(dtype) for _ in range(3)]
+    return t
+
+
+def to_u16(t):
+    return t.contiguous().view(_torch().int16).numpy().view(np.uint16)
+
+
+def code(dtype):
+    torch = _torch()
+    return 0 if dtype == torch.float16 else 1
+
+
+def run_gpu(engine, q, k, v, BM, BN):
+    torch = _torch()
+    Q, K, V = (x.cuda() for x in (q, k, v))
+    O = engine.attn(Q, K, V, BM=BM, BN=BN)
+    torch.cuda.synchronize()
+    rc, site = engine.get_status(0)
+    assert rc == 0, f"device status {site:#x}"
+    return O.cpu()
+
+
+def compare(oracle_mod, got_u16, ref_u16, dt):
+    a = oracle_mod.to_f32(got_u16, dt)
+    b = oracle_mod.to_f32(ref_u16, dt)
+    assert np.isfinite(a).all()
+    d = np.abs(a - b)
+    return float(d.max()), float(d.mean())
+
+
+@pytest.mark.parametrize("BM,BN", TILES)
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_parity_small(engine, oracle_mod, BM, BN, D, dt):
+    torch = _torch()
+    dtype = torch.float16 if dt == "f16" else torch.bfloat16
+    B, H, S = 1, 2, 512
+    q, k, v = make_inputs(B, H, S, D, dtype, seed=BM * 7 + BN + D)
+    out = run_gpu(engine, q, k, v, BM, BN)
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN, dtype=code(dtype))
+    mx, mean = compare(oracle_mod, to_u16(out), ref, code(dtype))
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.parametrize("S", [1, 17, 129, 200, 333, 1000])
+@pytest.mark.parametrize("BM,BN", [(128, 128), (256, 128), (128, 256), (256, 32)])
+def test_parity_ragged_tails(engine, oracle_mod, S, BM, BN):
+    """S not a multiple of BM or BN: key columns >= S are masked, rows >= S are
+    not written (the reference's tail semantics, tuning/attn_test.cu:152-170)."""
+    torch = _torch()
+    q, k, v = make_inputs(2, 3, S, 128, torch.float16, seed=S)
+    out = run_gpu(engine, q, k, v, BM, BN)
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
+    mx, mean = compare(oracle_mod, to_u16(out), ref, 0)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=lambda p: p.stem)
+def test_kernel_vs_reference_golden(engine, oracle_mod, path):
+    """The kernel on the reference's own fixture inputs against the output the
+    reference's host attention produced (tests/golden)."""
+    torch = _torch()
+    z = np.load(path)
+    B, H, S, D, BM, BN = (int(x) for x in z["meta"])
+    q, k, v = (torch.from_numpy(z[n].astype(np.uint16).view(np.int16)).view(torch.float16)
+               for n in ("q", "k", "v"))
+    for bm, bn in ((128, BN), (256, min(BN, 128))):
+        out = run_gpu(engine, q, k, v, bm, bn)
+        mx, mean = compare(oracle_mod, to_u16(out), z["o_ref"], 0)
+        assert mx <= MAX_ABS and mean <= MEAN_ABS, (bm, bn, mx, mean)
+
+
+def test_padded_layout_reads_and_writes_only_valid_rows(engine, oracle_mod):
+    torch = _torch()
+    B, H, S, D, BM, BN = 1, 2, 300, 128, 256, 128
+    SQO, SKV = 512, 384
+    q, k, v = make_inputs(B, H, S, D, torch.float16, seed=5)
+    Qp = torch.full((B, H, SQO, D), float("nan"), dtype=torch.float16)
+    Kp = torch.full((B, H, SKV, D), float("nan"), dtype=torch.float16)
+    Vp = torch.full((B, H, SKV, D), float("nan"), dtype=torch.float16)
+    Qp[:, :, :S], Kp[:, :, :S], Vp[:, :, :S] = q, k, v
+    Op = torch.full((B, H, SQO, D), 7.0, dtype=torch.float16).cuda()
+    engine.attn_padded(Qp.cuda(), Kp.cuda(), Vp.cuda(), Op, S, BM=BM, BN=BN)
+    torch.cuda.synchronize()
+    assert engine.get_status(0)[0] == 0
+    O = Op.cpu()
+    assert torch.all(O[:, :, S:] == 7.0), "padding rows of O were written"
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
+    mx, mean = compare(oracle_mod, to_u16(O[:, :, :S]), ref, 0)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS
+
+
+def test_constant_v_gives_constant_o(engine):
+    """softmax rows sum to one: V = c everywhere gives O = c (up to rounding of c)."""
+    torch = _torch()
+    B, H, S, D = 1, 4, 4096, 128
+    q, k, _ = make_inputs(B, H, S, D, torch.float16, seed=9)
+    v = torch.full((B, H, S, D), 0.3125, dtype=torch.float16)
+    out = run_gpu(engine, q, k, v, 256, 128).float()
+    assert torch.allclose(out, torch.full_like(out, 0.3125), atol=2e-3)
+
+
+def test_key_permutation_invariance(engine):
+    """Permuting keys and values together leaves O unchanged (within rounding)."""
+    torch = _torch()
+    B, H, S, D = 1, 2, 2048, 128
+    q, k, v = make_inputs(B, H, S, D, torch.float16, seed=11)
+    perm = torch.randperm(S, generator=torch.Generator().manual_seed(3))
+    a = run_gpu(engine, q, k, v, 256, 128).float()
+    b = run_gpu(engine, q, k[:, :, perm], v[:, :, perm], 256, 128).float()
+    assert (a - b).abs().max().item() <= 2e-3
+
+
+def test_repeat_calls_are_deterministic(engine):
+    torch = _torch()
+    q, k, v = make_inputs(1, 4, 1024, 128, torch.float16, seed=12)
+    a = run_gpu(engine, q, k, v, 256, 128)
+    b = run_gpu(engine, q, k, v, 256, 128)
+    assert torch.equal(a, b)
