@@ -38,14 +38,18 @@ class AttnError(RuntimeError):
 
 
 def lib() -> ctypes.CDLL:
-    """Load libattnprof.so (raises if it has not been built)."""
+    """Load libattnprof.so (raises if it has not been built).  ATTNPROF_LIB may
+    name another build of the same library (e.g. one compiled with other
+    tuning macros)."""
     global _lib
     if _lib is None:
-        if not Path(LIB_PATH).exists():
+        import os
+        path = Path(os.environ.get("ATTNPROF_LIB", str(LIB_PATH)))
+        if not path.exists():
             raise RuntimeError(
                 f"{LIB_PATH} is missing: build it with `python -m attnprofile_b200._build` "
                 "(there is no CPU fallback)")
-        L = ctypes.CDLL(str(LIB_PATH))
+        L = ctypes.CDLL(str(path))
         vp, i, u64p = ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_ulonglong)
         L.attn_fwd.argtypes = [vp, vp, vp, vp, i, i, i, i, i, i, i, vp]
         L.attn_fwd_padded.argtypes = [vp, vp, vp, vp, i, i, i, i, i, i, i, i, i, vp]
@@ -137,8 +141,9 @@ def profile_layout() -> tuple[int, int]:
 
 def attn_profiled(Q, K, V, O=None, *, BM: int = 256, BN: int = 128, cta: int = 0, stream=None):
     """One launch of the profiler-enabled variant; returns (O, stamps) where
-    stamps is an int64 CPU tensor [6 phases, 32 slots, 2] of clock64 values
-    (0 = not recorded).  Phases: LoadQ, LoadK, LoadV, GEMM-QK, SOFTMAX, GEMM-PV."""
+    stamps is an int64 CPU tensor [10 phases, 32 slots, 2] of clock64 values
+    (0 = not recorded).  Phases: LoadQ, LoadK, LoadV, GEMM-QK, SOFTMAX, GEMM-PV,
+    then the SOFTMAX steps S-ld, max, exp, P-st."""
     import torch
     if O is None:
         O = torch.empty_like(Q)

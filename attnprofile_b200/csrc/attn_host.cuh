@@ -23,7 +23,7 @@
 #include <mutex>
 #include <unordered_map>
 
-#include "../../include/attnprof.h"
+#include "attnprof.h"
 #include "attn_kernel.cuh"
 
 namespace attnprof {

@@ -57,9 +57,15 @@ enum : int {
 // clock64 stamps, the first kProfSlots KV iterations.  The phases are those of
 // the reference's profiler (attn.cu:5-22): LoadQ, LoadK, LoadV, GEMM-QK,
 // SOFTMAX, GEMM-PV.
-constexpr int kProfPhases = 6;
+// Four more phases split SOFTMAX of the profiled warp into its steps: the S
+// load from TMEM, the row max (and lazy-rescale decision), the exponentials
+// with the P stores issued, and the wait for the P stores to land.
+constexpr int kProfPhases = 10;
 constexpr int kProfSlots = 32;
-enum : int { kPhLoadQ = 0, kPhLoadK = 1, kPhLoadV = 2, kPhQK = 3, kPhSoftmax = 4, kPhPV = 5 };
+enum : int {
+  kPhLoadQ = 0, kPhLoadK = 1, kPhLoadV = 2, kPhQK = 3, kPhSoftmax = 4, kPhPV = 5,
+  kPhSmLoadS = 6, kPhSmMax = 7, kPhSmExp = 8, kPhSmStoreP = 9
+};
 
 struct AttnParams {
   int S;                       // logical sequence length (rows of Q and of K/V per head)
@@ -127,9 +133,14 @@ struct AttnConfig {
   static constexpr int BAR_KV_FULL = BAR_Q + NQ;
   static constexpr int BAR_KV_EMPTY = BAR_KV_FULL + STAGES;
   static constexpr int BAR_S_FULL = BAR_KV_EMPTY + STAGES;  // [NQ][NSBUF]
-  static constexpr int BAR_P_READY = BAR_S_FULL + NQ * NSBUF;
-  static constexpr int BAR_O_DONE = BAR_P_READY + NQ;
-  static constexpr int BAR_DRAIN = BAR_O_DONE + NQ;
+  // P is published in PHALVES parts (P V of part h may start once part h is
+  // in TMEM).  One part: with the stale-max softmax below, P is final only
+  // after the whole row has been checked against the lazy-rescale threshold.
+  static constexpr int PHALVES = 1;
+  static constexpr int BAR_P_READY = BAR_S_FULL + NQ * NSBUF;      // [NQ][NSBUF][PHALVES]
+  static constexpr int BAR_O_DONE = BAR_P_READY + NQ * NSBUF * PHALVES;  // every P V of tile i
+  static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
+  static constexpr int BAR_DRAIN = BAR_O_FINAL + NQ;
   static constexpr int NUM_BARS = BAR_DRAIN + 1;
 
   static constexpr int OFF_MISC = OFF_BAR + ((NUM_BARS * 8 + 15) / 16) * 16;
@@ -142,6 +153,13 @@ struct AttnConfig {
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;
   static constexpr int OBSERVER_WARP = NUM_SOFTMAX_WARPS + 2;  // profiler only
   static constexpr int NUM_THREADS = 32 * (NUM_SOFTMAX_WARPS + 4);
+  // Register split for NQ = 2 (384 threads launched at 168 registers each =
+  // 64512): softmax warpgroups 2 x 128 x 192 + producer/MMA warpgroup
+  // 128 x 120 = 64512.
+  static constexpr uint32_t REG_SOFTMAX = 192;
+  static constexpr uint32_t REG_OTHER = 120;
+  static_assert(NQ != 2 || 2 * 128 * REG_SOFTMAX + 128 * REG_OTHER <= 384 * 168,
+                "register split exceeds the launch allocation");
 
   static constexpr uint32_t IDESC_S = ptx::idesc_f16(128, BN, kBF16, false);
   static constexpr uint32_t IDESC_PV = ptx::idesc_f16(128, D, kBF16, true);
@@ -153,13 +171,52 @@ struct AttnConfig {
 // accumulators all hold exactly enough.
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
+// Of every 8 (column-pair) exponentials in a softmax chunk, this many run as
+// the FMA-pipe polynomial (ptx::exp2_poly) and the rest on the MUFU unit, so
+// the two pipes share the B*H*S^2 exponentials.
+#ifndef ATTNPROF_POLY_PAIRS_OF_8
+#define ATTNPROF_POLY_PAIRS_OF_8 0
+#endif
+constexpr int kPolyPairsOf8 = ATTNPROF_POLY_PAIRS_OF_8;
+
+// Which column pairs of a 32-column chunk take the polynomial: spread evenly
+// (e.g. 4 of 8 -> every other pair) so both pipes stay busy.
+__host__ __device__ constexpr bool poly_pair(int e) {
+  return kPolyPairsOf8 > 0 && ((e % 8) * kPolyPairsOf8) % 8 + kPolyPairsOf8 > 7;
+}
+
+// Row maximum of N register values with independent partial maxima (short
+// dependency chains; max is exact, so the order does not change the result).
+template <int N>
+__device__ __forceinline__ float row_max(const uint32_t* r, float init) {
+  static_assert(N % 8 == 0, "");
+  float a[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = __uint_as_float(r[k]);
+  int c = 8;
+#pragma unroll
+  for (; c + 16 <= N; c += 16) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      a[k] = ptx::fmax3(a[k], __uint_as_float(r[c + k]), __uint_as_float(r[c + 8 + k]));
+  }
+  if (c < N) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = fmaxf(a[k], __uint_as_float(r[c + k]));
+  }
+  const float b0 = ptx::fmax3(a[0], a[1], a[2]);
+  const float b1 = ptx::fmax3(a[3], a[4], a[5]);
+  const float b2 = ptx::fmax3(a[6], a[7], init);
+  return ptx::fmax3(b0, b1, b2);
+}
+
 struct WaitCtx {
   volatile int* abort;  // CTA-local abort flag in shared memory
   int* status;
   unsigned long long timeout_ns;
 };
 
-static __device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity, const WaitCtx& w,
+static __device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity, const WaitCtx& w,
                                            int site) {
   const unsigned long long t0 = ptx::globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
@@ -276,43 +333,61 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const AttnParams& p, con
   if (ok) prof.stamp(kPhLoadQ, 0, 1);
 
   int t = 0;
-  auto ring_wait = [&](int& stage) -> bool {
+  // Wait for ring item t (K_j when is_k, else V_j) to land in its slot.
+  auto ring_wait = [&](int& stage, bool is_k, int j) -> bool {
     stage = t % C::STAGES;
     const bool r = wait_bar(bar(C::BAR_KV_FULL + stage), (t / C::STAGES) & 1, w, kSiteKvFull);
     ++t;
-    if (r) ptx::tc_fence_after();
+    if (r) {
+      prof.stamp(is_k ? kPhLoadK : kPhLoadV, j, 1);
+      ptx::tc_fence_after();
+    }
     return r;
   };
 
-  // S_i(j) = Q_i K_j^T : D/16 MMAs of 128 x BN x 16.
+  // Descriptors are built once; per MMA only byte offsets >> 4 are added to
+  // the start-address field (bits 0-13; no carry out of it because every
+  // operand lies below 256 KB of shared memory).  Per-k-step offsets are
+  // compile-time constants, the slot offset is added once per GEMM.
+  constexpr int KSTEPS_S = C::D / 16;
+  uint64_t qd0[C::NQ];
+#pragma unroll
+  for (int i = 0; i < C::NQ; ++i)
+    qd0[i] = ptx::smem_desc_sw128(sbase + C::OFF_Q + i * C::Q_TILE_BYTES, 16, 1024);
+  const uint64_t kd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, 16, 1024);
+  const uint64_t vd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, C::KV_BLK_BYTES, 1024);
+  auto slot_off = [](int stage) -> uint64_t {
+    return static_cast<uint64_t>((stage * C::KV_TILE_BYTES) >> 4);
+  };
+
+  // S_i(j) = Q_i K_j^T : D/16 MMAs of 128 x BN x 16.  K-step kk reads 16
+  // elements (32 B) of every 128 B row of 64-column block kk / 4.
   auto issue_s = [&](int i, int j, int stage) {
     const uint32_t d_tmem = tmem + (i * C::NSBUF + j % C::NSBUF) * C::BN;
-    const uint32_t qa = sbase + C::OFF_Q + i * C::Q_TILE_BYTES;
-    const uint32_t kb = sbase + C::OFF_KV + stage * C::KV_TILE_BYTES;
+    const uint64_t kd = kd0 + slot_off(stage);
 #pragma unroll
-    for (int kk = 0; kk < C::D / 16; ++kk) {
-      const uint32_t koff = (kk & 3) * 32u;  // 16 elements = 32 B inside the 128 B row
-      const uint64_t ad = ptx::smem_desc_sw128(qa + (kk >> 2) * C::Q_BLK_BYTES + koff, 16, 1024);
-      const uint64_t bd = ptx::smem_desc_sw128(kb + (kk >> 2) * C::KV_BLK_BYTES + koff, 16, 1024);
-      ptx::mma_ss(d_tmem, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
+    for (int kk = 0; kk < KSTEPS_S; ++kk) {
+      const uint64_t qo = static_cast<uint64_t>(((kk >> 2) * C::Q_BLK_BYTES + (kk & 3) * 32) >> 4);
+      const uint64_t ko = static_cast<uint64_t>(((kk >> 2) * C::KV_BLK_BYTES + (kk & 3) * 32) >> 4);
+      ptx::mma_ss(d_tmem, qd0[i] + qo, kd + ko, C::IDESC_S, kk > 0 ? 1u : 0u);
     }
   };
-  // O_i += P_i(j) V_j : BN/16 MMAs of 128 x D x 16, A = P from TMEM.
-  auto issue_pv = [&](int i, int j, int stage) {
+  // O_i += P_i(j) V_j : BN/16 MMAs of 128 x D x 16, A = P from TMEM; K-step
+  // kk reads 16 rows (keys) = two 1024 B atoms of V.
+  auto issue_pv = [&](int i, int j, int stage, int k0, int k1) {
     const uint32_t p_tmem = tmem + (i * C::NSBUF + j % C::NSBUF) * C::BN;
     const uint32_t o_tmem = tmem + C::TMEM_O_COL + i * C::D;
-    const uint32_t vb = sbase + C::OFF_KV + stage * C::KV_TILE_BYTES;
+    const uint64_t vd = vd0 + slot_off(stage);
 #pragma unroll
-    for (int kk = 0; kk < C::BN / 16; ++kk) {
-      const uint64_t bd = ptx::smem_desc_sw128(vb + kk * 2048u, C::KV_BLK_BYTES, 1024);
-      ptx::mma_ts(o_tmem, p_tmem + kk * 8, bd, C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
-    }
+    for (int kk = k0; kk < k1; ++kk)
+      ptx::mma_ts(o_tmem, p_tmem + kk * 8, vd + static_cast<uint64_t>(kk * 2048 >> 4),
+                  C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
   };
 
   // Prologue: S for the first NSBUF KV tiles.
   for (int jj = 0; jj < C::NSBUF && jj < n && ok; ++jj) {
     int sk;
-    if (!(ok = ring_wait(sk))) break;
+    if (!(ok = ring_wait(sk, true, jj))) break;
     for (int i = 0; i < C::NQ; ++i) {
       if (i == 0) prof.stamp(kPhQK, jj, 0);
       issue_s(i, jj, sk);
@@ -323,17 +398,24 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const AttnParams& p, con
 
   for (int j = 0; j < n && ok; ++j) {
     int sv;
-    if (!(ok = ring_wait(sv))) break;
+    if (!(ok = ring_wait(sv, false, j))) break;
     const int jn = j + C::NSBUF;
     int sk = -1;
     for (int i = 0; i < C::NQ && ok; ++i) {
-      if (!(ok = wait_bar(bar(C::BAR_P_READY + i), j & 1, w, kSitePReady))) break;
-      ptx::tc_fence_after();
-      if (i == 0) prof.stamp(kPhPV, j, 0);
-      issue_pv(i, j, sv);
+      const int pb = C::BAR_P_READY + (i * C::NSBUF + j % C::NSBUF) * C::PHALVES;
+      constexpr int KSTEPS = C::BN / 16;
+#pragma unroll
+      for (int h = 0; h < C::PHALVES; ++h) {
+        if (!(ok = wait_bar(bar(pb + h), (j / C::NSBUF) & 1, w, kSitePReady))) break;
+        ptx::tc_fence_after();
+        if (i == 0 && h == 0) prof.stamp(kPhPV, j, 0);
+        issue_pv(i, j, sv, h * KSTEPS / C::PHALVES, (h + 1) * KSTEPS / C::PHALVES);
+      }
+      if (!ok) break;
       ptx::mma_commit(bar(C::BAR_O_DONE + i));
+      if (j == n - 1) ptx::mma_commit(bar(C::BAR_O_FINAL + i));
       if (jn < n) {
-        if (sk < 0 && !(ok = ring_wait(sk))) break;
+        if (sk < 0 && !(ok = ring_wait(sk, true, jn))) break;
         if (i == 0) prof.stamp(kPhQK, jn, 0);
         issue_s(i, jn, sk);
         ptx::mma_commit(bar(C::BAR_S_FULL + i * C::NSBUF + jn % C::NSBUF));
@@ -387,9 +469,11 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
     if (rec) {
       prof.stamp(kPhQK, j, 1);
       prof.stamp(kPhSoftmax, j, 0);
+      prof.stamp(kPhSmLoadS, j, 0);
     }
 
     const int lim = p.S - j * C::BN;  // valid key columns in this tile
+    const int pbar = C::BAR_P_READY + (qi * C::NSBUF + buf) * C::PHALVES;
     float mx = -INFINITY;
     constexpr int KEEP = C::BN <= 128;
     constexpr int NCH = C::BN / 32;
@@ -403,24 +487,28 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       }
       ptx::tmem_wait_ld();
       ptx::reg_fence(sreg);
+      if (rec) {
+        prof.stamp(kPhSmLoadS, j, 1);
+        prof.stamp(kPhSmMax, j, 0);
+      }
       if (lim < C::BN) {
 #pragma unroll
         for (int c = 0; c < C::BN; ++c)
           if (c >= lim) sreg[c] = __float_as_uint(-INFINITY);
       }
-#pragma unroll
-      for (int c = 0; c < C::BN; ++c) mx = fmaxf(mx, __uint_as_float(sreg[c]));
+      mx = row_max<C::BN>(sreg, mx);
     } else {
 #pragma unroll 1
       for (int c = 0; c < NCH; ++c) {
         ptx::tmem_ld32(lane_base + s_col + c * 32, sreg);
         ptx::tmem_wait_ld();
         ptx::reg_fence(sreg);
+        if (lim < C::BN) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float v = (c * 32 + e < lim) ? __uint_as_float(sreg[e]) : -INFINITY;
-          mx = fmaxf(mx, v);
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= lim) sreg[e] = __float_as_uint(-INFINITY);
         }
+        mx = row_max<32>(sreg, mx);
       }
     }
 
@@ -451,9 +539,15 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       }
     }
 
+    if (rec) {
+      prof.stamp(kPhSmMax, j, 1);
+      prof.stamp(kPhSmExp, j, 0);
+    }
     // P = exp2(s * scale_log2 - m * scale_log2), packed to T pairs over S.
     const float neg = -m_run * sl2;
-    float sum = 0.f;
+    const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
+    const uint64_t negx2 = ptx::f2_pack(neg, neg);
+    uint64_t part[2] = {0ull, 0ull};  // packed partial row sums (4 short FADD chains)
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       if constexpr (!KEEP) {
@@ -470,17 +564,43 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int c0 = (KEEP ? c * 32 : 0) + 2 * e;
-        const float p0 = ptx::ex2_approx(fmaf(__uint_as_float(sreg[c0]), sl2, neg));
-        const float p1 = ptx::ex2_approx(fmaf(__uint_as_float(sreg[c0 + 1]), sl2, neg));
-        sum += p0 + p1;
+        // x = s * scale_log2 - m * scale_log2 for two columns in one f32x2 FMA
+        const uint64_t x2 = ptx::f2_fma(
+            ptx::f2_pack(__uint_as_float(sreg[c0]), __uint_as_float(sreg[c0 + 1])), sl2x2, negx2);
+        float x0, x1;
+        ptx::f2_unpack(x2, x0, x1);
+        float p0, p1;
+        if (poly_pair(e)) {
+          ptx::exp2_poly_x2(x0, x1, p0, p1);
+        } else {
+          p0 = ptx::ex2_approx(x0);
+          p1 = ptx::ex2_approx(x1);
+        }
+        part[e & 1] = ptx::f2_add(part[e & 1], ptx::f2_pack(p0, p1));
         pk[e] = pack2<T>(p0, p1);
       }
       ptx::tmem_st16(lane_base + s_col + c * 16, pk);
+      if (C::PHALVES == 2 && c == NCH / 2 - 1) {
+        // First half of P is in TMEM: let the MMA warp start P V on it.
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(pbar));
+      }
+    }
+    float sa, sb, sc_, sd;
+    ptx::f2_unpack(part[0], sa, sb);
+    ptx::f2_unpack(part[1], sc_, sd);
+    const float sum = (sa + sb) + (sc_ + sd);
+    if (rec) {
+      prof.stamp(kPhSmExp, j, 1);
+      prof.stamp(kPhSmStoreP, j, 0);
     }
     ptx::tmem_wait_st();
+    if (rec) prof.stamp(kPhSmStoreP, j, 1);
     ptx::tc_fence_before();
     __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(bar(C::BAR_P_READY + qi));
+    if (lane == 0) ptx::mbar_arrive(bar(pbar + C::PHALVES - 1));
     if (rec) prof.stamp(kPhSoftmax, j, 1);
     l_run = l_run * alpha + sum;
   }
@@ -491,7 +611,7 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
   // any timed-out wait before it returns) decides uniformly whether to store.
   ptx::named_bar_sync(1 + qi, 128);
   bool go = ok && (*w.abort == 0);
-  if (go) go = wait_bar(bar(C::BAR_O_DONE + qi), (n - 1) & 1, w, kSiteODone);
+  if (go) go = wait_bar(bar(C::BAR_O_FINAL + qi), 0, w, kSiteODone);
   go = __all_sync(0xffffffffu, go);
   const uint32_t stage_s = sbase + C::OFF_Q + qi * C::Q_TILE_BYTES;
   if (go) {
@@ -571,9 +691,11 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
       ptx::mbar_init(bar(C::BAR_KV_EMPTY + s), 1);
     }
     for (int i = 0; i < C::NQ * C::NSBUF; ++i) ptx::mbar_init(bar(C::BAR_S_FULL + i), 1);
-    for (int i = 0; i < C::NQ; ++i) {
+    for (int i = 0; i < C::NQ * C::NSBUF * C::PHALVES; ++i)
       ptx::mbar_init(bar(C::BAR_P_READY + i), 4);
+    for (int i = 0; i < C::NQ; ++i) {
       ptx::mbar_init(bar(C::BAR_O_DONE + i), 1);
+      ptx::mbar_init(bar(C::BAR_O_FINAL + i), 1);
     }
     ptx::mbar_init(bar(C::BAR_DRAIN), 1);
     *abort_flag = 0;
@@ -599,16 +721,18 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
   Prof<PROFILE> prof{(PROFILE && cta_lin == p.prof_cta) ? p.prof : nullptr};
 
   if (warp < C::NUM_SOFTMAX_WARPS) {
+    if constexpr (C::NQ == 2) ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
     softmax_role<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, q_row0, bh, p, w, prof);
-  } else if (warp == C::LOAD_WARP) {
-    if (lane == 0) load_role<C, PROFILE>(&tmQ, &tmK, &tmV, sbase, q_row0, bh, p, w, prof);
-    __syncwarp();
-  } else if (warp == C::MMA_WARP) {
-    if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, p, w, prof);
-    __syncwarp();
-  } else if (warp == C::OBSERVER_WARP) {
-    if constexpr (PROFILE) {
-      if (lane == 0 && prof.buf != nullptr) observer_role<C>(sbase, p, w, prof);
+  } else {
+    if constexpr (C::NQ == 2) ptx::setmaxnreg_dec<C::REG_OTHER>();
+    if (warp == C::LOAD_WARP) {
+      if (lane == 0) load_role<C, PROFILE>(&tmQ, &tmK, &tmV, sbase, q_row0, bh, p, w, prof);
+    } else if (warp == C::MMA_WARP) {
+      if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, p, w, prof);
+    } else if (warp == C::OBSERVER_WARP) {
+      if constexpr (PROFILE) {
+        if (lane == 0 && prof.buf != nullptr) observer_role<C>(sbase, p, w, prof);
+      }
     }
     __syncwarp();
   }

@@ -1,0 +1,116 @@
+"""Per-phase cycle profiler (post-processing on the host).
+
+Rebuilds the reference's clock64 phase profiler (attn.cu:3-38 ProfileResult /
+Profile, stamps attn.cu:133-444, host averaging and table printing in
+run_one_case attn.cu:1400-1494) on the phases of the B200 pipeline.  One CTA
+of the profiler-enabled kernel variant (attn_fwd_profiled) writes clock64
+begin/end stamps per KV iteration (first 32 iterations, one slot each):
+
+  LoadQ    producer issues the Q TMA            -> MMA warp sees Q landed
+  LoadK    producer issues K_j (slot free)      -> MMA warp sees K_j landed
+  LoadV    producer issues V_j (slot free)      -> MMA warp sees V_j landed
+  GEMM-QK  MMA warp issues S_0 = Q_0 K_j^T       -> softmax warp sees S_0 complete
+  SOFTMAX  softmax warp sees S_0                 -> P_0 written to TMEM and signalled
+  GEMM-PV  MMA warp issues O_0 += P_0 V_j        -> observer warp sees it complete
+
+(Tile 0 of the CTA; all stamps come from one SM's clock.)  SOFTMAX is also
+split into its steps: S-ld (tcgen05.ld of S and its wait), max (row max and
+the lazy-rescale decision), exp (exponentials, P stores issued) and P-st (wait
+for the P stores to land).  Unlike the
+reference's synchronous profiled kernel, the phases here overlap: a load or
+GEMM phase includes the time its consumer took to look.  `period` is the
+mean distance between consecutive SOFTMAX starts, i.e. cycles per KV
+iteration of the whole pipeline.
+
+    python -m attnprofile_b200.profiler [--s 4096] [--d 128] [--h 16]
+           [--tiles 256x128,128x128,...] [--runs 20]
+prints one markdown row per tile in the reference's table format
+(README.md:11-19: | BM | BN | LoadQ | LoadK | LoadV | GEMM-QK | SOFTMAX | GEMM-PV |).
+"""
+from __future__ import annotations
+
+import argparse
+
+PHASES = ["LoadQ", "LoadK", "LoadV", "GEMM-QK", "SOFTMAX", "GEMM-PV"]
+# Steps of SOFTMAX (same warp): S tcgen05.ld + wait, row max + rescale
+# decision, exponentials with the P tcgen05.st issued, wait for the P stores.
+SUBPHASES = ["S-ld", "max", "exp", "P-st"]
+ALL_PHASES = PHASES + SUBPHASES
+
+
+def summarize(stamps_list) -> dict:
+    """Mean cycles per phase over recorded slots and runs.
+
+    stamps_list: iterable of int64 arrays [6, 32, 2] (begin, end); 0 = unset."""
+    import numpy as np
+    sums = {p: [] for p in ALL_PHASES}
+    periods = []
+    for st in stamps_list:
+        a = np.asarray(st, dtype=np.int64)
+        for k, name in enumerate(ALL_PHASES[: a.shape[0]]):
+            b, e = a[k, :, 0], a[k, :, 1]
+            ok = (b != 0) & (e != 0) & (e >= b)
+            if name == "LoadQ":
+                ok[1:] = False
+            sums[name].extend((e[ok] - b[ok]).tolist())
+        sb = a[PHASES.index("SOFTMAX"), :, 0]
+        sb = sb[sb != 0]
+        if sb.size > 2:
+            periods.extend(np.diff(sb[1:]).tolist())  # skip the first (pipeline fill)
+    out = {p: (float(np.mean(v)) if v else float("nan")) for p, v in sums.items()}
+    out["period"] = float(np.mean(periods)) if periods else float("nan")
+    return out
+
+
+def run(B=1, H=16, S=4096, D=128, BM=256, BN=128, dtype="f16", runs=20, cta=None, seed=0):
+    import torch
+    import attnprofile_b200 as ap
+    dt = torch.float16 if dtype == "f16" else torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    Q, K, V = (torch.randn(B, H, S, D, generator=g, device="cuda").to(dt) for _ in range(3))
+    n_qt = (S + BM - 1) // BM
+    cta = (n_qt * B * H) // 2 if cta is None else cta  # a CTA from the middle of the grid
+    for _ in range(3):
+        ap.attn(Q, K, V, BM=BM, BN=BN)
+    stamps = []
+    for _ in range(runs):
+        _, st = ap.attn_profiled(Q, K, V, BM=BM, BN=BN, cta=cta)
+        stamps.append(st.numpy())
+    torch.cuda.synchronize()
+    rc, site = ap.get_status(torch.cuda.current_device())
+    if rc != 0:
+        raise RuntimeError(f"device status {site:#x}")
+    return summarize(stamps)
+
+
+def table_header() -> str:
+    cols = ["BM", "BN"] + PHASES + ["period"] + SUBPHASES
+    return "| " + " | ".join(cols) + " |\n|" + "---|" * len(cols)
+
+
+def table_row(BM, BN, r) -> str:
+    vals = [f"{r[p]:.0f}" for p in PHASES + ["period"] + SUBPHASES]
+    return f"| {BM} | {BN} | " + " | ".join(vals) + " |"
+
+
+def main(argv=None):
+    ap_ = argparse.ArgumentParser()
+    ap_.add_argument("--b", type=int, default=1)
+    ap_.add_argument("--h", type=int, default=16)
+    ap_.add_argument("--s", type=int, default=4096)
+    ap_.add_argument("--d", type=int, default=128)
+    ap_.add_argument("--dtype", default="f16")
+    ap_.add_argument("--tiles", default="256x128,128x128,256x64,128x64,128x256,256x32,128x32")
+    ap_.add_argument("--runs", type=int, default=20)
+    a = ap_.parse_args(argv)
+    print(f"B={a.b} H={a.h} S={a.s} D={a.d} {a.dtype}: cycles (clock64) per phase, "
+          f"mean over KV iterations 0-31 and {a.runs} runs")
+    print(table_header())
+    for t in a.tiles.split(","):
+        bm, bn = (int(x) for x in t.split("x"))
+        r = run(a.b, a.h, a.s, a.d, bm, bn, a.dtype, a.runs)
+        print(table_row(bm, bn, r), flush=True)
+
+
+if __name__ == "__main__":
+    main()

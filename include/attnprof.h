@@ -68,8 +68,9 @@ int attn_fwd_padded(const void* Q, const void* K, const void* V, void* O, int B,
  * attn_fwd_profiled -- attn_fwd with the per-phase cycle profiler compiled in
  * (f16 and bf16).  CTA number profile_cta (blockIdx.y * gridDim.x + blockIdx.x)
  * writes clock64 begin/end stamps for the phases LoadQ, LoadK, LoadV, GEMM-QK,
- * SOFTMAX, GEMM-PV of its first 32 KV iterations into dev_profile_buf, laid
- * out as u64 [6][32][2] (see attn_profile_layout).  The caller zeroes the
+ * SOFTMAX, GEMM-PV (then the SOFTMAX steps S-load, max, exp, P-store) of its
+ * first 32 KV iterations into dev_profile_buf, laid out as u64 [10][32][2]
+ * (see attn_profile_layout).  The caller zeroes the
  * buffer before the launch; unstamped slots stay 0.
  * Replaces: the clock64 profiler of attn.cu (ProfileResult attn.cu:5-22,
  *           stamps attn.cu:133-444, run_one_case attn.cu:1400-1494).
@@ -78,7 +79,7 @@ int attn_fwd_profiled(const void* Q, const void* K, const void* V, void* O, int 
                       int D, int dtype, int BM, int BN, void* stream,
                       unsigned long long* dev_profile_buf, int profile_cta);
 
-/* Profile buffer geometry: *phases = 6, *slots = 32 (u64 pairs). */
+/* Profile buffer geometry: *phases = 10, *slots = 32 (u64 pairs). */
 int attn_profile_layout(int* phases, int* slots);
 
 /*
