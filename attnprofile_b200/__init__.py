@@ -16,7 +16,8 @@ from ._build import LIB_PATH, build  # noqa: F401
 
 __all__ = [
     "AttnError", "attn", "attn_padded", "attn_profiled", "query_config", "get_status",
-    "set_timeout_ns", "debug_fault", "lib", "build", "ERR", "SUPPORTED_TILES",
+    "set_timeout_ns", "debug_fault", "lib", "build", "ERR", "SUPPORTED_TILES", "attn_sharded",
+    "shard_range",
 ]
 
 ERR = {
@@ -180,6 +181,25 @@ def set_timeout_ns(ns: int) -> None:
 
 def debug_fault(mode: int) -> None:
     _check(lib().attn_debug_fault(mode), "attn_debug_fault")
+
+
+def attn_sharded(Qs, Ks, Vs, Os, devices, *, B: int, H: int, BM: int = 256, BN: int = 128):
+    """(batch, head)-sharded attention over several GPUs of this process.
+
+    Qs[g] etc. hold GPU g's units contiguously ([1, units_g, S, D] on
+    devices[g]; units_g from shard_range(B*H, len(devices), g)).  Launches on
+    every device, joins them all, and raises AttnError with the first error.
+    Returns the per-device kernel times in ms."""
+    n = len(devices)
+    S, D = Qs[0].shape[2], Qs[0].shape[3]
+    vp = ctypes.c_void_p
+    arr = lambda ts: (vp * n)(*[vp(t.data_ptr()) for t in ts])
+    devs = (ctypes.c_int * n)(*devices)
+    ms = (ctypes.c_float * n)()
+    rc = lib().attn_fwd_sharded(n, devs, arr(Qs), arr(Ks), arr(Vs), arr(Os), B, H, S, D,
+                                _dtype_code(Qs[0]), BM, BN, ms)
+    _check(rc, "attn_fwd_sharded")
+    return list(ms)
 
 
 def shard_range(units: int, n_dev: int, g: int) -> tuple[int, int]:

@@ -23,7 +23,11 @@
 #include <mutex>
 #include <unordered_map>
 
+#if __has_include("attnprof.h")
 #include "attnprof.h"
+#else
+#include "../../include/attnprof.h"  // builds without -I include (the tuning-harness driver)
+#endif
 #include "attn_kernel.cuh"
 
 namespace attnprof {

@@ -100,7 +100,7 @@ struct AttnConfig {
   static constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
 
   static_assert(D == 64 || D == 128, "head dim must be 64 or 128");
-  static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN must be 32/64/128/256");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
   static_assert(NQ == 1 || NQ == 2, "NQ must be 1 or 2");
   static_assert(STAGES >= 2, "need at least two K/V slots");
 
@@ -133,10 +133,11 @@ struct AttnConfig {
   static constexpr int BAR_KV_FULL = BAR_Q + NQ;
   static constexpr int BAR_KV_EMPTY = BAR_KV_FULL + STAGES;
   static constexpr int BAR_S_FULL = BAR_KV_EMPTY + STAGES;  // [NQ][NSBUF]
-  // P is published in PHALVES parts (P V of part h may start once part h is
-  // in TMEM).  One part: with the stale-max softmax below, P is final only
-  // after the whole row has been checked against the lazy-rescale threshold.
-  static constexpr int PHALVES = 1;
+  // P is published in PHALVES parts so P V can start on the first keys while
+  // the softmax computes the rest: with >= 2 chunks of 32 columns, part 0 is
+  // the first PSPLIT_CHUNKS chunks (P V K-steps [0, 2 * PSPLIT_CHUNKS)).
+  static constexpr int PHALVES = BN >= 64 ? 2 : 1;
+  static constexpr int PSPLIT_CHUNKS = BN / 64;
   static constexpr int BAR_P_READY = BAR_S_FULL + NQ * NSBUF;      // [NQ][NSBUF][PHALVES]
   static constexpr int BAR_O_DONE = BAR_P_READY + NQ * NSBUF * PHALVES;  // every P V of tile i
   static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
@@ -409,7 +410,8 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const AttnParams& p, con
         if (!(ok = wait_bar(bar(pb + h), (j / C::NSBUF) & 1, w, kSitePReady))) break;
         ptx::tc_fence_after();
         if (i == 0 && h == 0) prof.stamp(kPhPV, j, 0);
-        issue_pv(i, j, sv, h * KSTEPS / C::PHALVES, (h + 1) * KSTEPS / C::PHALVES);
+        constexpr int KSPLIT = C::PHALVES == 2 ? 2 * C::PSPLIT_CHUNKS : KSTEPS;
+        issue_pv(i, j, sv, h == 0 ? 0 : KSPLIT, h == 0 ? KSPLIT : KSTEPS);
       }
       if (!ok) break;
       ptx::mma_commit(bar(C::BAR_O_DONE + i));
@@ -580,7 +582,7 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
         pk[e] = pack2<T>(p0, p1);
       }
       ptx::tmem_st16(lane_base + s_col + c * 16, pk);
-      if (C::PHALVES == 2 && c == NCH / 2 - 1) {
+      if (C::PHALVES == 2 && c == C::PSPLIT_CHUNKS - 1) {
         // First half of P is in TMEM: let the MMA warp start P V on it.
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
@@ -670,6 +672,11 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV,
                     const __grid_constant__ CUtensorMap tmO, const AttnParams p) {
+// The body uses sm_100a-only instructions (tcgen05, setmaxnreg): it is
+// compiled for the arch-specific target only.  A build that also emits
+// generic compute_100 PTX (nvcc -arch=sm_100a does) gets an empty kernel there,
+// which a B200 never runs because the sm_100a binary matches it.
+#if defined(__CUDA_ARCH_FEAT_SM100_ALL) || !defined(__CUDA_ARCH__)
   using C = AttnConfig<T, D, BN, NQ, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = ptx::smem_u32(smem_raw);
@@ -743,6 +750,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, C::TMEM_ALLOC);
   }
+#endif
 }
 
 }  // namespace attnprof

@@ -1,0 +1,102 @@
+"""B200 resource model for the tuning harness's BM/BN sweep.
+
+Same interface as the reference's tuning/solver.py (solve / solve_reuse,
+tuning/solver.py:376-411, and the keys its callers read: BM, BN, NumSmem,
+NumSmemP, RepeatN, SmemSize, RegSize, EstimatedRegsPerThread), so
+tuning/benchmark_run_attn.py picks it up unchanged through
+`from solver import solve` when this directory comes first on sys.path.
+
+The constraints are those of the sm_100a kernel (attnprofile_b200/csrc/
+attn_kernel.cuh, AttnConfig) instead of the Hopper wgmma/register model of the
+reference (tuning/solver.py:14-132):
+
+  * BM in {128, 256}: one or two 128-row Q tiles per CTA (MMA M = 128);
+    RepeatN = BM / 128 (KernelIdx 1/2 -> 128, 3 -> 256, as the harness's
+    get_configs expects, tuning/benchmark_run_attn.py:76-84);
+  * BN a multiple of 32 in [32, 256] (32-column softmax chunks, TMA box <= 256);
+  * tensor memory: NQ * NSBUF * BN + NQ * HD <= 512 columns, NSBUF = 2 when
+    one Q tile and the doubled S buffer fit, else 1;
+  * shared memory: Q tiles + STAGES K/V slots (STAGES = 2 * NumSmem, the
+    driver's mapping) + barriers + alignment slack <= SmemLimit;
+  * registers are not a constraint (fixed split per variant): the estimate is
+    reported as 240 so the harness keeps one consumer-register setting.
+"""
+from __future__ import annotations
+
+TMEM_COLS = 512
+MMA_M_B200 = 128
+
+
+def tmem_columns(BM: int, BN: int, HD: int) -> int:
+    nq = BM // MMA_M_B200
+    nsbuf = 2 if (nq == 1 and 2 * BN + HD <= TMEM_COLS) else 1
+    return nq * nsbuf * BN + nq * HD
+
+
+def smem_bytes(BM: int, BN: int, HD: int, stages: int) -> int:
+    """Dynamic shared memory of the kernel variant (mirrors AttnConfig)."""
+    nq = BM // MMA_M_B200
+    nsbuf = 2 if (nq == 1 and 2 * BN + HD <= TMEM_COLS) else 1
+    phalves = 2 if BN >= 64 else 1
+    off_bar = nq * 128 * HD * 2 + stages * BN * HD * 2
+    num_bars = nq + 2 * stages + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1
+    off_misc = off_bar + ((num_bars * 8 + 15) // 16) * 16
+    return off_misc + 16 + 1024
+
+
+def _solve(HD=64, NumSmem=2, MMA_M=64, MMA_K=16, NumConsumer=2, ElementWidth=2,
+           SmemLimit=232_448, KernelIdx=2, ConsumerRegLimit=240):
+    if HD not in (64, 128) or ElementWidth != 2:
+        return []
+    stages = max(2, 2 * NumSmem)
+    bms = [256] if KernelIdx == 3 else [128]
+    solutions = []
+    for BM in bms:
+        for BN in range(32, 257, 32):
+            if tmem_columns(BM, BN, HD) > TMEM_COLS:
+                continue
+            size = smem_bytes(BM, BN, HD, stages)
+            if size > SmemLimit:
+                continue
+            regs = 240
+            solutions.append({
+                "BM": BM,
+                "BN": BN,
+                "NumSmem": NumSmem,
+                # P lives in tensor memory on B200; the harness only needs 0
+                # for kernel 1 and a nonzero multiple of 4 for kernels 2/3.
+                "NumSmemP": 0 if KernelIdx == 1 else 4,
+                "RepeatN": BM // MMA_M_B200,
+                "SmemSize": size,
+                "RegSize": regs * (BM // MMA_M_B200) * 128 * 4,
+                "TmemCols": tmem_columns(BM, BN, HD),
+                "EstimatedRegsPerThread": regs,
+                "ConservativeRegsPerThread": regs,
+                "CombinedRegs": regs,
+                "QKStageRegs": regs,
+                "PVStageRegs": regs,
+            })
+    return solutions
+
+
+def solve(HD: int = 64, NumSmem: int = 2, MMA_M: int = 64, MMA_K: int = 16,
+          NumConsumer: int = 2, ElementWidth: int = 2, SmemLimit: int = 232_448,
+          KernelIdx: int = 2, ConsumerRegLimit: int = 240):
+    """Feasible (BM, BN) tiles of the B200 kernel for head dim HD."""
+    return _solve(HD, NumSmem, MMA_M, MMA_K, NumConsumer, ElementWidth, SmemLimit, KernelIdx,
+                  ConsumerRegLimit)
+
+
+def solve_reuse(HD: int = 64, NumSmem: int = 2, MMA_M: int = 64, MMA_K: int = 16,
+                NumConsumer: int = 2, ElementWidth: int = 2, SmemLimit: int = 232_448,
+                KernelIdx: int = 2, ConsumerRegLimit: int = 240):
+    """Same as solve(): the B200 model has no separate register-reuse variant."""
+    return solve(HD, NumSmem, MMA_M, MMA_K, NumConsumer, ElementWidth, SmemLimit, KernelIdx,
+                 ConsumerRegLimit)
+
+
+if __name__ == "__main__":
+    for hd in (64, 128):
+        for k in (1, 3):
+            for s in solve(HD=hd, NumSmem=2, KernelIdx=k):
+                print(hd, k, s["BM"], s["BN"], s["SmemSize"], s["TmemCols"])

@@ -239,6 +239,7 @@ def main():
     import torch
     import torch.distributed as dist
     import attnprofile_b200 as ap
+    from attnprofile_b200 import shard
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -260,7 +261,7 @@ def main():
     S, D, H = w["S"], w["D"], w["H"]
     tdt = torch.float16 if w["dtype"] == "f16" else torch.bfloat16
     units_total = cfg["B"] * H
-    u0, u1 = ap.shard_range(units_total, n, rank)
+    u0, u1 = shard.shard_range(units_total, n, rank)
     units = u1 - u0
     elt = 2
     set_bytes = 4 * units * S * D * elt
@@ -269,13 +270,7 @@ def main():
     # Seeded inputs, generated per global unit so a unit's data does not depend
     # on the number of GPUs.
     def gen_set(s):
-        Q = torch.empty(1, units, S, D, dtype=tdt, device=dev)
-        K, V = torch.empty_like(Q), torch.empty_like(Q)
-        for i, u in enumerate(range(u0, u1)):
-            g = torch.Generator(device=dev).manual_seed(args.seed * 1000003 + s * 7919 + u)
-            for t in (Q, K, V):
-                t[0, i].copy_((torch.randn(S, D, generator=g, device=dev) * w["sigma"]).to(tdt))
-        return Q, K, V, torch.empty_like(Q)
+        return shard.generate_units(u0, u1, S, D, tdt, dev, args.seed, s, w["sigma"])
 
     sets = [gen_set(s) for s in range(n_sets)]
     torch.cuda.synchronize()
@@ -318,10 +313,7 @@ def main():
     if rc != 0:
         raise SystemExit(f"device status after timing: {rc} site {site:#x}")
 
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = shard.max_over_ranks(ms, dev)
     total_flops = flops(units_total, S, D) * args.steps
     value = total_flops / (ms_max * 1e-3) / 1e12
 
@@ -363,17 +355,13 @@ def main():
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": flops(units_total, S, D) * steps_e / (float(te.item()) * 1e-3) / 1e12,
+        te = shard.max_over_ranks(e0.elapsed_time(e1), dev)
+        e2e = {"value": flops(units_total, S, D) * steps_e / (te * 1e-3) / 1e12,
                "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * hq.numel() * elt,
                "d2h_bytes_per_step": ho.numel() * elt, "steps": steps_e,
                "api": "attnprofile_b200.attn -> attn_fwd (C ABI)"}
 
-    launches = torch.tensor([args.steps], dtype=torch.int64, device=dev)
-    if world > 1:
-        dist.all_reduce(launches)
+    launches = shard.sum_over_ranks(args.steps, dev)
 
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
@@ -394,7 +382,7 @@ def main():
                          "peak_source": f"{kind} {'sustained' if peak == sustained else 'burst'}"
                                         " bf16 cuBLAS (MEASURED_PEAKS.json)",
                          "kernel": "attn_fwd_kernel"},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches.item()),
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

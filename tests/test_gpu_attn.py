@@ -167,3 +167,21 @@ def test_repeat_calls_are_deterministic(engine):
     a = run_gpu(engine, q, k, v, 256, 128)
     b = run_gpu(engine, q, k, v, 256, 128)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("BM,BN", [(256, 128), (128, 128), (128, 256), (128, 64), (256, 32)])
+@pytest.mark.parametrize("ramp", ["up", "down"])
+def test_parity_moving_row_max(engine, oracle_mod, BM, BN, ramp):
+    """Keys scaled by a ramp over the sequence.  'up' makes the row max grow by
+    far more than the lazy-rescale threshold from tile to tile (P recomputed,
+    O rescaled many times); 'down' puts the max in the first tile (no rescale
+    after it)."""
+    torch = _torch()
+    S = 2048
+    q, k, v = make_inputs(1, 2, S, 128, torch.float16, seed=21)
+    r = torch.linspace(0.5, 6.0, S) if ramp == "up" else torch.linspace(6.0, 0.5, S)
+    k = (k.float() * r.view(1, 1, S, 1)).half()
+    out = run_gpu(engine, q, k, v, BM, BN)
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
+    mx, mean = compare(oracle_mod, to_u16(out), ref, 0)
+    assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
