@@ -6,7 +6,7 @@
 // accumulators in TMEM, tcgen05.ld/st, tcgen05.commit onto mbarriers, TMA
 // tile loads and stores, and bounded mbarrier waits.
 //
-// No load here carries a cluster multicast qualifier: every TMA load reads
+// Every TMA load here is a plain single-destination copy: it reads
 // this GPU's own global memory into this CTA's own shared memory.
 #pragma once
 
@@ -83,7 +83,7 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 }
 
 // ----------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), 3-D tiles, no multicast
+// TMA (cp.async.bulk.tensor), 3-D tiles, single destination
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

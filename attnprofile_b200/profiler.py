@@ -25,7 +25,8 @@ iteration of the whole pipeline.
     python -m attnprofile_b200.profiler [--s 4096] [--d 128] [--h 16]
            [--tiles 256x128,128x128,...] [--runs 20]
 prints one markdown row per tile in the reference's table format
-(README.md:11-19: | BM | BN | LoadQ | LoadK | LoadV | GEMM-QK | SOFTMAX | GEMM-PV |).
+(the reference project's README.md:11-19:
+| BM | BN | LoadQ | LoadK | LoadV | GEMM-QK | SOFTMAX | GEMM-PV |).
 """
 from __future__ import annotations
 

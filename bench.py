@@ -42,8 +42,9 @@ WORKLOADS = {
     "c4": dict(B=8, H=32, S=8192, D=128, dtype="bf16", sigma=1.0, scaling="strong"),
     "c5": dict(B=1, H=64, S=32768, D=128, dtype="f16", sigma=0.5, scaling="strong"),
 }
-# Published reference figures for the same metric and shape (Hopper, 114 SMs;
-# README.md:333-337 for C2, README.md:265-270 for C3).  None elsewhere.
+# The reference's published figures for the same metric and shape (Hopper,
+# 114 SMs; the reference project's README.md:333-337 for C2 and
+# README.md:265-270 for C3).  None for the other shapes.
 PUBLISHED = {"c2": 309.022, "c3": 296.931}
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "attn fwd TFLOP/s (4*B*H*S^2*D/t)"
@@ -157,7 +158,7 @@ def cpu_baseline_reference(wl):
     from oracle import oracle
     exe = oracle.ref_binary()
     cfg = {"c2": "c2head", "c3": "c3head"}.get(wl, "c2head")
-    threads = max(1, min(os.cpu_count() or 1, 16))
+    threads = max(1, min(len(os.sched_getaffinity(0)), 16))
     if not exe.exists():
         return None
     r = subprocess.run([str(exe), "time", cfg, str(threads)], capture_output=True, text=True,
@@ -194,7 +195,8 @@ def run_reference_arm(args):
     g = torch.Generator().manual_seed(args.seed)
     q, k, v = ((torch.randn(Bs, H, S, D, generator=g) * w["sigma"]).to(tdt)
                .view(torch.int16).numpy().view(np.uint16) for _ in range(3))
-    threads = oracle.max_threads()
+    # every host core (torchrun sets OMP_NUM_THREADS=1 per rank; override it)
+    threads = len(os.sched_getaffinity(0))
     rows_per_step = 1024
     rng = np.random.default_rng(args.seed)
 
