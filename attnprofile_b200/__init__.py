@@ -67,9 +67,14 @@ def lib() -> ctypes.CDLL:
         L.attn_error_string.argtypes = [i]
         L.attn_error_string.restype = ctypes.c_char_p
         L.attn_debug_fault.argtypes = [i]
+        ll, llp = ctypes.c_longlong, ctypes.POINTER(ctypes.c_longlong)
+        L.attn_set_split.argtypes = [i]
+        L.attn_plan_split.argtypes = [ll, i, ll, i, ctypes.POINTER(i), llp, llp]
+        L.attn_query_split.argtypes = [i, i, i, i, i, i, i, ctypes.POINTER(i), llp, llp, u64p]
         for name in ("attn_fwd", "attn_fwd_padded", "attn_fwd_profiled", "attn_fwd_sharded",
                      "attn_shard_range", "attn_get_status", "attn_query_config",
-                     "attn_profile_layout", "attn_debug_fault", "attn_version"):
+                     "attn_profile_layout", "attn_debug_fault", "attn_version",
+                     "attn_set_split", "attn_plan_split", "attn_query_split"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -142,9 +147,10 @@ def profile_layout() -> tuple[int, int]:
 
 def attn_profiled(Q, K, V, O=None, *, BM: int = 256, BN: int = 128, cta: int = 0, stream=None):
     """One launch of the profiler-enabled variant; returns (O, stamps) where
-    stamps is an int64 CPU tensor [10 phases, 32 slots, 2] of clock64 values
+    stamps is an int64 CPU tensor [11 phases, 32 slots, 2] of clock64 values
     (0 = not recorded).  Phases: LoadQ, LoadK, LoadV, GEMM-QK, SOFTMAX, GEMM-PV,
-    then the SOFTMAX steps S-ld, max, exp, P-st."""
+    then the SOFTMAX steps S-ld, max, exp, P-st (slots = KV iterations), then
+    Epilogue (slots = steps, profiler.EPILOGUE_STEPS)."""
     import torch
     if O is None:
         O = torch.empty_like(Q)
@@ -200,6 +206,33 @@ def attn_sharded(Qs, Ks, Vs, Os, devices, *, B: int, H: int, BM: int = 256, BN: 
                                 _dtype_code(Qs[0]), BM, BN, ms)
     _check(rc, "attn_fwd_sharded")
     return list(ms)
+
+
+def set_split(mode: int) -> None:
+    """Key split of the last wave for later launches: 0 automatic (default),
+    1 never, 2..4 force that many key ranges per unit of the last wave."""
+    _check(lib().attn_set_split(int(mode)), "attn_set_split")
+
+
+def plan_split(units: int, num_kv_tiles: int, slots: int, mode: int = 0) -> dict:
+    """The host planner alone (no GPU): how `units` (B*H*ceil(S/BM)) units
+    with `num_kv_tiles` key tiles each run on `slots` resident CTAs."""
+    k, whole, ctas = ctypes.c_int(), ctypes.c_longlong(), ctypes.c_longlong()
+    _check(lib().attn_plan_split(units, num_kv_tiles, slots, mode, ctypes.byref(k),
+                                 ctypes.byref(whole), ctypes.byref(ctas)), "attn_plan_split")
+    return {"split": k.value, "whole": whole.value, "ctas": ctas.value}
+
+
+def query_split(B: int, H: int, S: int, D: int, *, BM: int = 256, BN: int = 128,
+                dtype: int = DTYPE_F16) -> dict:
+    """The plan a launch of this shape uses on the current device, with its
+    workspace size in bytes (needs a GPU)."""
+    k, whole, ctas = ctypes.c_int(), ctypes.c_longlong(), ctypes.c_longlong()
+    ws = ctypes.c_ulonglong()
+    _check(lib().attn_query_split(B, H, S, D, dtype, BM, BN, ctypes.byref(k), ctypes.byref(whole),
+                                  ctypes.byref(ctas), ctypes.byref(ws)), "attn_query_split")
+    return {"split": k.value, "whole": whole.value, "ctas": ctas.value,
+            "workspace_bytes": ws.value}
 
 
 def shard_range(units: int, n_dev: int, g: int) -> tuple[int, int]:

@@ -17,6 +17,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -44,12 +46,112 @@ constexpr int auto_stages(int cap = 8) {
   return best;
 }
 
+// How the units (BM query rows of one (batch, head)) of one launch are laid
+// out over CTAs: `whole` units run over all key tiles, the other
+// units - whole are each split into `split` key ranges.
+struct SplitPlan {
+  int split = 1;
+  long long units = 0, whole = 0, ctas = 0;
+  size_t ws_bytes = 0;           // workspace for the split units (0: none)
+  size_t off_ml = 0, off_cnt = 0, cnt_bytes = 0;
+};
+
 struct LaunchOpts {
   unsigned long long timeout_ns = 2000000000ull;  // bounded-wait limit: 2 s
   int fault_mode = 0;
   unsigned long long* prof = nullptr;
   int prof_cta = 0;
+  int split = 0;                 // 0: automatic, 1: never split, k >= 2: split k ways
+  void* workspace = nullptr;     // caller-provided workspace (else stream-ordered pool)
+  size_t workspace_bytes = 0;
+  SplitPlan* plan_out = nullptr; // receives the plan
+  bool plan_only = false;        // compute the plan, launch nothing
 };
+
+// Chooses the key split of the last, partially filled wave of units.  A
+// wave of `slots` CTAs (SMs x resident CTAs per SM) runs one unit each; when
+// units % slots leaves a partial wave, those units can instead run as k key
+// ranges each (more, shorter CTAs), with the last range of each unit merging
+// the k partial results.  Cost model in KV-tile periods, fitted to B200
+// measurements (1x{1,2,4,6,16}x{1024..16384}x128, BM 256, BN 128): a whole
+// unit costs n_kv + 2; a part ceil(n_kv / k) + 4 + k (its prologue and
+// epilogue, the partial-O write and count-in, and the merge of k partials by
+// the last part, which grows with k); a split launch adds 3 (workspace
+// allocation and counter reset).  The split is taken when it saves at least
+// 5 %.  It pays for few, long units (1x2x8192: 1.6x faster), not for a second
+// wave of many (1x16x4096 stays unsplit).  mode: 0 automatic, 1 never,
+// k >= 2 forced (when units % slots == 0, the last full wave is split).
+inline SplitPlan plan_split(long long units, int n_kv, long long slots, int mode) {
+  SplitPlan pl;
+  pl.units = pl.whole = pl.ctas = units;
+  if (mode == 1 || units <= 0 || n_kv < 2 || slots <= 0) return pl;
+  const long long full = units / slots, rem = units % slots;
+  const int kmax = std::min(kMaxSplit, n_kv);
+  if (mode >= 2) {
+    const long long nsplit = rem ? rem : std::min(units, slots);
+    pl.split = std::min(mode, kmax);
+    pl.whole = units - nsplit;
+    pl.ctas = pl.whole + nsplit * pl.split;
+    return pl;
+  }
+  if (rem == 0) return pl;
+  double best = 0.95 * static_cast<double>(full + 1) * (n_kv + 2);
+  for (int k = 2; k <= kmax; ++k) {
+    const long long waves = (rem * k + slots - 1) / slots;
+    const double c = static_cast<double>(full) * (n_kv + 2) +
+                     static_cast<double>(waves) * ((n_kv + k - 1) / k + 4 + k) + 3.0;
+    if (c < best) {
+      best = c;
+      pl.split = k;
+    }
+  }
+  if (pl.split > 1) {
+    pl.whole = full * slots;
+    pl.ctas = pl.whole + rem * pl.split;
+  }
+  return pl;
+}
+
+// Workspace of a plan: partial O (pt_bytes per element), (max, sum) per row,
+// one counter per (split unit, 128-row Q tile).  Each part 256-byte aligned.
+inline void plan_workspace(SplitPlan* pl, int BM, int D, int NQ, size_t pt_bytes) {
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  if (pl->split <= 1) return;
+  const size_t nsplit = static_cast<size_t>(pl->units - pl->whole);
+  const size_t rows = nsplit * pl->split * BM;
+  pl->off_ml = up(rows * D * pt_bytes);
+  pl->off_cnt = pl->off_ml + up(rows * sizeof(float2));
+  pl->cnt_bytes = nsplit * NQ * sizeof(int);
+  pl->ws_bytes = pl->off_cnt + up(pl->cnt_bytes);
+}
+
+// Stream-ordered workspace from a per-device pool that keeps its memory
+// (release threshold at the maximum), so steady-state calls map no pages.
+inline int workspace_acquire(size_t bytes, cudaStream_t st, void** out) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ATTN_ERR_CUDA;
+  cudaMemPool_t pool;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (pools[dev] == nullptr) {
+      cudaMemPoolProps props{};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      if (cudaMemPoolCreate(&pools[dev], &props) != cudaSuccess) {
+        pools[dev] = nullptr;
+        return ATTN_ERR_CUDA;
+      }
+      unsigned long long keep = ULLONG_MAX;
+      cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    pool = pools[dev];
+  }
+  if (cudaMallocFromPoolAsync(out, bytes, pool, st) != cudaSuccess) return ATTN_ERR_RESOURCE;
+  return ATTN_OK;
+}
 
 // ---------------------------------------------------------------------------
 // Driver entry point for cuTensorMapEncodeTiled (no link-time libcuda).
@@ -140,7 +242,34 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   static_assert(C::SMEM_BYTES <= kSmemLimit, "shared memory over the sm_100 per-CTA limit");
   const int dtype = std::is_same<T, __half>::value ? ATTN_DTYPE_F16 : ATTN_DTYPE_BF16;
   const long long BH = static_cast<long long>(B) * H;
-  if (BH > 65535) return ATTN_ERR_INVALID_ARG;  // grid.y limit
+  if (BH > 65535) return ATTN_ERR_INVALID_ARG;
+
+  auto kern = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE>;
+  static bool attr_done[64] = {};
+  static int slots_of[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return ATTN_ERR_CUDA;
+  if (dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
+        cudaSuccess)
+      return ATTN_ERR_RESOURCE;
+    int sms = 0, occ = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, C::NUM_THREADS, C::SMEM_BYTES) !=
+            cudaSuccess)
+      return ATTN_ERR_CUDA;
+    if (occ < 1) return ATTN_ERR_RESOURCE;
+    slots_of[dev] = sms * occ;
+    attr_done[dev] = true;
+  }
+  const long long qt = (S + C::BM - 1) / C::BM;
+  const int n_kv = (S + BN - 1) / BN;
+  SplitPlan plan = plan_split(BH * qt, n_kv, dev < 64 ? slots_of[dev] : 148, o.split);
+  plan_workspace(&plan, C::BM, D, NQ, sizeof(float));
+  if (o.plan_out) *o.plan_out = plan;
+  if (o.plan_only) return ATTN_OK;
+  if (plan.ctas > INT_MAX || qt > INT_MAX) return ATTN_ERR_INVALID_ARG;
+
   CUtensorMap mq, mk, mv, mo;
   int rc;
   if ((rc = get_tensor_map(&mq, Q, dtype, D, S, static_cast<int>(BH), q_rows, C::QROWS))) return rc;
@@ -148,19 +277,15 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   if ((rc = get_tensor_map(&mv, V, dtype, D, S, static_cast<int>(BH), kv_rows, BN))) return rc;
   if ((rc = get_tensor_map(&mo, O, dtype, D, S, static_cast<int>(BH), q_rows, C::QROWS))) return rc;
 
-  auto kern = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE>;
-  static bool attr_done[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return ATTN_ERR_CUDA;
-  if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
-        cudaSuccess)
-      return ATTN_ERR_RESOURCE;
-    attr_done[dev] = true;
-  }
   AttnParams p;
   p.S = S;
-  p.num_kv_tiles = (S + BN - 1) / BN;
+  p.num_kv_tiles = n_kv;
+  p.qt_per_bh = static_cast<int>(qt);
+  p.num_whole = static_cast<int>(plan.whole);
+  p.split = plan.split;
+  p.ws_o = nullptr;
+  p.ws_ml = nullptr;
+  p.ws_cnt = nullptr;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(D)));
   p.status = device_status_ptr();
   if (p.status == nullptr) return ATTN_ERR_CUDA;
@@ -168,11 +293,31 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   p.fault_mode = o.fault_mode;
   p.prof = o.prof;
   p.prof_cta = o.prof_cta;
-  const dim3 grid((S + C::BM - 1) / C::BM, static_cast<unsigned>(BH), 1);
-  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, mo, p);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return ATTN_ERR_CUDA;
-  return ATTN_OK;
+
+  uint8_t* ws = nullptr;
+  bool pooled = false;
+  if (plan.split > 1) {
+    if (o.workspace != nullptr) {
+      if (o.workspace_bytes < plan.ws_bytes) return ATTN_ERR_RESOURCE;
+      ws = static_cast<uint8_t*>(o.workspace);
+    } else {
+      void* w = nullptr;
+      if ((rc = workspace_acquire(plan.ws_bytes, stream, &w))) return rc;
+      ws = static_cast<uint8_t*>(w);
+      pooled = true;
+    }
+    p.ws_o = reinterpret_cast<float4*>(ws);
+    p.ws_ml = reinterpret_cast<float2*>(ws + plan.off_ml);
+    p.ws_cnt = reinterpret_cast<int*>(ws + plan.off_cnt);
+    if (cudaMemsetAsync(p.ws_cnt, 0, plan.cnt_bytes, stream) != cudaSuccess) rc = ATTN_ERR_CUDA;
+  }
+  if (rc == ATTN_OK) {
+    kern<<<static_cast<unsigned>(plan.ctas), C::NUM_THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv,
+                                                                                     mo, p);
+    if (cudaGetLastError() != cudaSuccess) rc = ATTN_ERR_CUDA;
+  }
+  if (pooled && cudaFreeAsync(ws, stream) != cudaSuccess && rc == ATTN_OK) rc = ATTN_ERR_CUDA;
+  return rc;
 }
 
 }  // namespace attnprof

@@ -60,16 +60,36 @@ enum : int {
 // Four more phases split SOFTMAX of the profiled warp into its steps: the S
 // load from TMEM, the row max (and lazy-rescale decision), the exponentials
 // with the P stores issued, and the wait for the P stores to land.
-constexpr int kProfPhases = 10;
+// The last phase, Epilogue, is stamped once per CTA by the same warp, its
+// slots holding steps instead of iterations: 0 the whole epilogue (loop exit
+// to the O store issued, or to the exit of a part that does not merge),
+// 1 the wait for the last P V, 2 the partial-O write of a split part,
+// 3 its count-in, 4 the merge (split) or the O normalisation into shared
+// memory (whole unit), 5 the TMA store issue.
+constexpr int kProfPhases = 11;
 constexpr int kProfSlots = 32;
 enum : int {
   kPhLoadQ = 0, kPhLoadK = 1, kPhLoadV = 2, kPhQK = 3, kPhSoftmax = 4, kPhPV = 5,
-  kPhSmLoadS = 6, kPhSmMax = 7, kPhSmExp = 8, kPhSmStoreP = 9
+  kPhSmLoadS = 6, kPhSmMax = 7, kPhSmExp = 8, kPhSmStoreP = 9, kPhEpilogue = 10
+};
+enum : int {
+  kEpAll = 0, kEpWaitO = 1, kEpPartial = 2, kEpCount = 3, kEpMerge = 4, kEpStore = 5
 };
 
 struct AttnParams {
   int S;                       // logical sequence length (rows of Q and of K/V per head)
   int num_kv_tiles;            // ceil(S / BN)
+  // Work decomposition (1-D grid).  Unit u = bh * qt_per_bh + q tile (BM rows
+  // of one (batch, head)).  CTAs [0, num_whole) run units 0 .. num_whole-1
+  // over all KV tiles; each remaining unit is split into `split` key ranges
+  // (1 < split <= kMaxSplit, split <= num_kv_tiles), one CTA each, merged by
+  // whichever of them finishes last.  No split: num_whole = all units.
+  int qt_per_bh;
+  int num_whole;
+  int split;
+  float4* ws_o;                // [split units][split][D / 4][BM] (float4 columns of partial O)
+  float2* ws_ml;               // [split units][split][BM]: (row max in raw score units, row sum)
+  int* ws_cnt;                 // [split units][NQ]: parts finished; zero between launches
   float scale_log2;            // log2(e) / sqrt(D)
   int* status;                 // device status word (0 = ok)
   unsigned long long timeout_ns;
@@ -77,6 +97,37 @@ struct AttnParams {
   unsigned long long* prof;    // PROFILE builds: stamp buffer, may be null
   int prof_cta;                // linear CTA index to profile
 };
+
+constexpr int kMaxSplit = 4;
+
+// What one CTA computes: BM query rows of one (batch, head) against key tiles
+// [kv_lo, kv_lo + n); part < 0 for a whole unit, else its slot in the workspace.
+struct WorkTile {
+  int bh, q_row0, kv_lo, n, part;
+  long long slot;  // (split unit index) * split + part, for partial units
+};
+
+__device__ __forceinline__ WorkTile work_tile_of(int cta, int BM, const AttnParams& p) {
+  WorkTile t;
+  int u;
+  if (cta < p.num_whole) {
+    u = cta;
+    t.part = -1;
+    t.kv_lo = 0;
+    t.n = p.num_kv_tiles;
+    t.slot = 0;
+  } else {
+    const int r = cta - p.num_whole;
+    u = p.num_whole + r / p.split;
+    t.part = r % p.split;
+    t.kv_lo = static_cast<int>(static_cast<long long>(t.part) * p.num_kv_tiles / p.split);
+    t.n = static_cast<int>(static_cast<long long>(t.part + 1) * p.num_kv_tiles / p.split) - t.kv_lo;
+    t.slot = static_cast<long long>(r);
+  }
+  t.bh = u / p.qt_per_bh;
+  t.q_row0 = (u % p.qt_per_bh) * BM;
+  return t;
+}
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi);
@@ -90,6 +141,14 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+
+// Partial O of a split unit in the workspace: f32 (a 16-bit partial adds a
+// second rounding of the output's own size; one f16 ulp is 3.9e-3 for |O| in
+// [4, 8), above the 2e-3 parity bound), as float4 columns (float4 number
+// (col / 4) * BM + row of the unit's block), so the 32 lanes of a warp (32
+// consecutive rows) touch 512 contiguous bytes per access.  Stores are plain
+// (they stay in L2 for the merging CTA); the merge loads them with
+// ld.global.cg (L2, past L1), since other CTAs wrote them.
 
 template <typename T, int D_, int BN_, int NQ_, int STAGES_>
 struct AttnConfig {
@@ -154,6 +213,9 @@ struct AttnConfig {
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;
   static constexpr int OBSERVER_WARP = NUM_SOFTMAX_WARPS + 2;  // profiler only
   static constexpr int NUM_THREADS = 32 * (NUM_SOFTMAX_WARPS + 4);
+  // One 128-row Q tile with narrow key tiles fits two CTAs per SM (shared
+  // and tensor memory); the register budget is capped to keep that possible.
+  static constexpr int MIN_CTAS_PER_SM = (NQ == 1 && BN <= 64) ? 2 : 1;
   // Register split for NQ = 2 (384 threads launched at 168 registers each =
   // 64512): softmax warpgroups 2 x 128 x 192 + producer/MMA warpgroup
   // 128 x 120 = 64512.
@@ -258,10 +320,11 @@ struct Prof {
 // ----------------------------------------------------------------------------
 template <class C, bool PROFILE>
 __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const CUtensorMap* tmV,
-                          uint32_t sbase, int q_row0, int bh, const AttnParams& p,
+                          uint32_t sbase, const WorkTile& wt, const AttnParams& p,
                           const WaitCtx& w, const Prof<PROFILE>& prof) {
   auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
-  const int n = p.num_kv_tiles;
+  const int n = wt.n;
+  const int q_row0 = wt.q_row0, bh = wt.bh;
   const uint64_t pol_kv = ptx::l2_policy_evict_last();
   const uint64_t pol_q = ptx::l2_policy_evict_first();
 
@@ -295,7 +358,7 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
 #pragma unroll
     for (int d = 0; d < C::DBLK; ++d)
       ptx::tma_load_3d_hint(dst + d * C::KV_BLK_BYTES, is_k ? tmK : tmV, bar(C::BAR_KV_FULL + s),
-                            d * 64, j * C::BN, bh, pol_kv);
+                            d * 64, (wt.kv_lo + j) * C::BN, bh, pol_kv);
     last_issued[s] = t;
     ++t;
   };
@@ -324,10 +387,10 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
 // MMA issuer (single thread)
 // ----------------------------------------------------------------------------
 template <class C, bool PROFILE>
-__device__ void mma_role(uint32_t tmem, uint32_t sbase, const AttnParams& p, const WaitCtx& w,
-                         const Prof<PROFILE>& prof) {
+__device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, const AttnParams& p,
+                         const WaitCtx& w, const Prof<PROFILE>& prof) {
   auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
-  const int n = p.num_kv_tiles;
+  const int n = wt.n;
   bool ok = true;
 
   for (int i = 0; i < C::NQ && ok; ++i) ok = wait_bar(bar(C::BAR_Q + i), 0, w, kSiteQ);
@@ -444,15 +507,16 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const AttnParams& p, con
 // ----------------------------------------------------------------------------
 template <typename T, class C, bool PROFILE>
 __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sgen,
-                             const CUtensorMap* tmO, int q_row0, int bh, const AttnParams& p,
+                             const CUtensorMap* tmO, const WorkTile& wt, const AttnParams& p,
                              const WaitCtx& w, const Prof<PROFILE>& prof) {
+  const int q_row0 = wt.q_row0, bh = wt.bh;
   auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
   const int wi = (threadIdx.x / 32) & 3;  // warp within the warpgroup = TMEM lane quarter
   const int lane = threadIdx.x & 31;
   const int row = wi * 32 + lane;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(wi * 32) << 16);
   const uint32_t o_col = C::TMEM_O_COL + qi * C::D;
-  const int n = p.num_kv_tiles;
+  const int n = wt.n;
   const float sl2 = p.scale_log2;
   const bool rec = PROFILE && qi == 0 && wi == 0 && lane == 0;
 
@@ -474,7 +538,7 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       prof.stamp(kPhSmLoadS, j, 0);
     }
 
-    const int lim = p.S - j * C::BN;  // valid key columns in this tile
+    const int lim = p.S - (wt.kv_lo + j) * C::BN;  // valid key columns in this tile
     const int pbar = C::BAR_P_READY + (qi * C::NSBUF + buf) * C::PHALVES;
     float mx = -INFINITY;
     constexpr int KEEP = C::BN <= 128;
@@ -611,42 +675,190 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
   // Every warp of the group reaches both named barriers, also after a failed
   // wait, so no warp can be left behind at a barrier; the abort flag (set by
   // any timed-out wait before it returns) decides uniformly whether to store.
+  if (rec) prof.stamp(kPhEpilogue, kEpAll, 0);
   ptx::named_bar_sync(1 + qi, 128);
   bool go = ok && (*w.abort == 0);
+  if (rec) prof.stamp(kPhEpilogue, kEpWaitO, 0);
   if (go) go = wait_bar(bar(C::BAR_O_FINAL + qi), 0, w, kSiteODone);
   go = __all_sync(0xffffffffu, go);
+  if (rec) prof.stamp(kPhEpilogue, kEpWaitO, 1);
   const uint32_t stage_s = sbase + C::OFF_Q + qi * C::Q_TILE_BYTES;
-  if (go) {
-    ptx::tc_fence_after();
-    const float inv = 1.f / l_run;
-    uint8_t* stage_g = sgen + C::OFF_Q + qi * C::Q_TILE_BYTES;
-#pragma unroll 1
-    for (int c = 0; c < C::D / 32; ++c) {
-      uint32_t o[32];
-      ptx::tmem_ld32(lane_base + o_col + c * 32, o);
-      ptx::tmem_wait_ld();
-      ptx::reg_fence(o);
-      const int dblk = (c * 32) / 64;
-      const int chunk0 = ((c * 32) % 64) / 8;  // first 16-byte chunk of these 32 columns
+  uint8_t* stage_g = sgen + C::OFF_Q + qi * C::Q_TILE_BYTES;
+  // Writes 16 output values (columns 16b .. 16b+15) of this thread's row
+  // into the 128B-swizzled staging tile (layout of the TMA box {64, QROWS}).
+  auto stage16 = [&](int b, const float* v) {
+    const int dblk = (b * 16) / 64;
+    const int chunk0 = ((b * 16) % 64) / 8;  // first 16-byte chunk of these 16 columns
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 v;
-        v.x = pack2<T>(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
-        v.y = pack2<T>(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
-        v.z = pack2<T>(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
-        v.w = pack2<T>(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
-        const int chunk = (chunk0 + q) ^ (row & 7);
-        *reinterpret_cast<uint4*>(stage_g + dblk * C::Q_BLK_BYTES + row * 128 + chunk * 16) = v;
+    for (int q = 0; q < 2; ++q) {
+      uint4 u;
+      u.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+      u.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+      u.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+      u.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+      const int chunk = (chunk0 + q) ^ (row & 7);
+      *reinterpret_cast<uint4*>(stage_g + dblk * C::Q_BLK_BYTES + row * 128 + chunk * 16) = u;
+    }
+  };
+  auto stage32 = [&](int c, const float (&v)[32]) {
+    stage16(2 * c, v);
+    stage16(2 * c + 1, v + 16);
+  };
+  // This thread's row of O, normalised by its own row sum, 32 columns at a time.
+  auto own32 = [&](int c, float inv, float (&v)[32]) {
+    uint32_t o[32];
+    ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+    ptx::tmem_wait_ld();
+    ptx::reg_fence(o);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]) * inv;
+  };
+
+  if (wt.part >= 0) {
+    // One key range of a split unit.  Every part writes its normalised O rows
+    // and (row max, row sum) to the workspace, then counts itself in; the part
+    // that arrives last merges all of them and stores O like a whole unit.
+    // The merge adds the parts in a fixed order and recomputes its own rows
+    // exactly as written, so the output does not depend on which part is last.
+    const int rrow = qi * C::QROWS + row;  // row within the unit
+    const long long slot0 = wt.slot - wt.part;
+    // float4 column 0 of this row in the partial block of slot s
+    auto col0 = [&](long long s) { return p.ws_o + s * (C::BM * C::D / 4) + rrow; };
+    if (rec) prof.stamp(kPhEpilogue, kEpPartial, 0);
+    if (go) {
+      ptx::tc_fence_after();
+      const float inv = 1.f / l_run;
+      float4* dst = col0(wt.slot);
+#pragma unroll 1
+      for (int b = 0; b < C::D / 16; ++b) {
+        uint32_t o[16];
+        ptx::tmem_ld16(lane_base + o_col + b * 16, o);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(o);
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          dst[(b * 4 + t) * C::BM] =
+              make_float4(__uint_as_float(o[4 * t + 0]) * inv, __uint_as_float(o[4 * t + 1]) * inv,
+                          __uint_as_float(o[4 * t + 2]) * inv, __uint_as_float(o[4 * t + 3]) * inv);
+      }
+      p.ws_ml[wt.slot * C::BM + rrow] = make_float2(m_run, l_run);
+      __threadfence();
+    }
+    if (rec) {
+      prof.stamp(kPhEpilogue, kEpPartial, 1);
+      prof.stamp(kPhEpilogue, kEpCount, 0);
+    }
+    volatile int* last_flag = reinterpret_cast<volatile int*>(sgen + C::OFF_MISC + 8) + qi;
+    ptx::named_bar_sync(1 + qi, 128);
+    if (row == 0) {
+      int last = 0;
+      if (*w.abort == 0) {
+        int* cnt = p.ws_cnt + (slot0 / p.split) * C::NQ + qi;
+        last = atomicAdd(cnt, 1) == p.split - 1;
+        if (last) {
+          __threadfence();
+          *cnt = 0;  // ready for the next launch
+        }
+      }
+      *last_flag = last;
+    }
+    ptx::named_bar_sync(1 + qi, 128);
+    if (rec) prof.stamp(kPhEpilogue, kEpCount, 1);
+    if (*last_flag == 0) {  // uniform over the warpgroup
+      if (rec) prof.stamp(kPhEpilogue, kEpAll, 1);
+      return;
+    }
+    if (rec) prof.stamp(kPhEpilogue, kEpMerge, 0);
+
+    float wgt[kMaxSplit], mq[kMaxSplit];
+    float mmax = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kMaxSplit; ++q) {
+      if (q < p.split) {
+        const float2 ml = q == wt.part ? make_float2(m_run, l_run)
+                                       : __ldcg(p.ws_ml + (slot0 + q) * C::BM + rrow);
+        mq[q] = ml.x;
+        wgt[q] = ml.y;
+        mmax = fmaxf(mmax, ml.x);
       }
     }
+    float tot = 0.f;
+#pragma unroll
+    for (int q = 0; q < kMaxSplit; ++q) {
+      if (q < p.split) {
+        wgt[q] *= ptx::ex2_approx((mq[q] - mmax) * sl2);
+        tot += wgt[q];
+      }
+    }
+    const float inv_tot = 1.f / tot;
+    const float inv_own = 1.f / l_run;
+    // 16 columns at a time: the loads of every other part are issued before
+    // any of them is used, so their L2 latencies overlap.
+#pragma unroll 1
+    for (int b = 0; b < C::D / 16; ++b) {
+      float4 rv[kMaxSplit][4];
+#pragma unroll
+      for (int q = 0; q < kMaxSplit; ++q) {
+        if (q < p.split && q != wt.part) {
+          const float4* src = col0(slot0 + q) + (b * 4) * C::BM;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) rv[q][t] = __ldcg(src + t * C::BM);
+        }
+      }
+      uint32_t o[16];  // this part's own values, recomputed exactly as written
+      ptx::tmem_ld16(lane_base + o_col + b * 16, o);
+      ptx::tmem_wait_ld();
+      ptx::reg_fence(o);
+      float acc[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+#pragma unroll
+      for (int q = 0; q < kMaxSplit; ++q) {
+        if (q < p.split) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float4 v =
+                q == wt.part
+                    ? make_float4(__uint_as_float(o[4 * t + 0]) * inv_own, __uint_as_float(o[4 * t + 1]) * inv_own,
+                                  __uint_as_float(o[4 * t + 2]) * inv_own, __uint_as_float(o[4 * t + 3]) * inv_own)
+                    : rv[q][t];
+            acc[4 * t + 0] = fmaf(wgt[q], v.x, acc[4 * t + 0]);
+            acc[4 * t + 1] = fmaf(wgt[q], v.y, acc[4 * t + 1]);
+            acc[4 * t + 2] = fmaf(wgt[q], v.z, acc[4 * t + 2]);
+            acc[4 * t + 3] = fmaf(wgt[q], v.w, acc[4 * t + 3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[e] *= inv_tot;
+      stage16(b, acc);
+    }
     ptx::fence_proxy_async_smem();
+    if (rec) prof.stamp(kPhEpilogue, kEpMerge, 1);
+  } else if (go) {
+    if (rec) prof.stamp(kPhEpilogue, kEpMerge, 0);
+    ptx::tc_fence_after();
+    const float inv = 1.f / l_run;
+#pragma unroll 1
+    for (int c = 0; c < C::D / 32; ++c) {
+      float v[32];
+      own32(c, inv, v);
+      stage32(c, v);
+    }
+    ptx::fence_proxy_async_smem();
+    if (rec) prof.stamp(kPhEpilogue, kEpMerge, 1);
   }
+  if (rec) prof.stamp(kPhEpilogue, kEpStore, 0);
   ptx::named_bar_sync(1 + qi, 128);
   if (wi == 0 && lane == 0 && *w.abort == 0) {
 #pragma unroll
     for (int d = 0; d < C::DBLK; ++d)
       ptx::tma_store_3d(tmO, stage_s + d * C::Q_BLK_BYTES, d * 64, q_row0 + qi * C::QROWS, bh);
     ptx::tma_store_commit();
+    if (rec) {
+      prof.stamp(kPhEpilogue, kEpStore, 1);
+      prof.stamp(kPhEpilogue, kEpAll, 1);
+    }
     ptx::tma_store_wait_read0();
   }
 }
@@ -654,10 +866,9 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
 // Profiler observer: stamps the completion of each P V of Q tile 0.  It only
 // watches; a missed phase costs a stamp, never an error status.
 template <class C>
-__device__ void observer_role(uint32_t sbase, const AttnParams& p, const WaitCtx& w,
-                              const Prof<true>& prof) {
+__device__ void observer_role(uint32_t sbase, int n, const WaitCtx& w, const Prof<true>& prof) {
   const uint32_t bar = sbase + C::OFF_BAR + 8u * (C::BAR_O_DONE + 0);
-  for (int j = 0; j < p.num_kv_tiles; ++j) {
+  for (int j = 0; j < n; ++j) {
     const unsigned long long t0 = ptx::globaltimer_ns();
     while (!ptx::mbar_try_wait(bar, j & 1)) {
       if (*w.abort || ptx::globaltimer_ns() - t0 > w.timeout_ns) return;
@@ -667,7 +878,8 @@ __device__ void observer_role(uint32_t sbase, const AttnParams& p, const WaitCtx
 }
 
 template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE>
-__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS, 1)
+__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
+                                  AttnConfig<T, D, BN, NQ, STAGES>::MIN_CTAS_PER_SM)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV,
@@ -684,8 +896,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
   uint8_t* sgen = smem_raw + (sbase - raw_s);
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const int q_row0 = blockIdx.x * C::BM;
-  const int bh = blockIdx.y;
+  const WorkTile wt = work_tile_of(blockIdx.x, C::BM, p);
 
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + C::OFF_MISC + 4);
@@ -729,16 +940,16 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
 
   if (warp < C::NUM_SOFTMAX_WARPS) {
     if constexpr (C::NQ == 2) ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
-    softmax_role<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, q_row0, bh, p, w, prof);
+    softmax_role<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, wt, p, w, prof);
   } else {
     if constexpr (C::NQ == 2) ptx::setmaxnreg_dec<C::REG_OTHER>();
     if (warp == C::LOAD_WARP) {
-      if (lane == 0) load_role<C, PROFILE>(&tmQ, &tmK, &tmV, sbase, q_row0, bh, p, w, prof);
+      if (lane == 0) load_role<C, PROFILE>(&tmQ, &tmK, &tmV, sbase, wt, p, w, prof);
     } else if (warp == C::MMA_WARP) {
-      if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, p, w, prof);
+      if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, wt, p, w, prof);
     } else if (warp == C::OBSERVER_WARP) {
       if constexpr (PROFILE) {
-        if (lane == 0 && prof.buf != nullptr) observer_role<C>(sbase, p, w, prof);
+        if (lane == 0 && prof.buf != nullptr) observer_role<C>(sbase, wt.n, w, prof);
       }
     }
     __syncwarp();

@@ -24,6 +24,7 @@ __device__ int g_attn_status;
 namespace {
 std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 std::atomic<int> g_fault_mode{0};
+std::atomic<int> g_split_mode{0};
 constexpr int kMaxDev = 64;
 std::mutex g_status_mu;
 int* g_status_ptr[kMaxDev] = {};
@@ -56,6 +57,10 @@ static int validate(const void* Q, const void* K, const void* V, const void* O, 
   return 1;  // proceed
 }
 
+static int dispatch(const void* Q, const void* K, const void* V, void* O, int B, int H, int S,
+                    int D, long long SQO, long long SKV, int dtype, int BM, int BN, cudaStream_t st,
+                    const LaunchOpts& o);
+
 static int run(const void* Q, const void* K, const void* V, void* O, int B, int H, int S, int D,
                long long SQO, long long SKV, int dtype, int BM, int BN, cudaStream_t st,
                unsigned long long* prof, int prof_cta) {
@@ -66,7 +71,14 @@ static int run(const void* Q, const void* K, const void* V, void* O, int B, int 
   o.fault_mode = g_fault_mode.load();
   o.prof = prof;
   o.prof_cta = prof_cta;
-  const bool pf = prof != nullptr;
+  o.split = g_split_mode.load();
+  return dispatch(Q, K, V, O, B, H, S, D, SQO, SKV, dtype, BM, BN, st, o);
+}
+
+static int dispatch(const void* Q, const void* K, const void* V, void* O, int B, int H, int S,
+                    int D, long long SQO, long long SKV, int dtype, int BM, int BN, cudaStream_t st,
+                    const LaunchOpts& o) {
+  const bool pf = o.prof != nullptr;
   if (dtype == ATTN_DTYPE_F16) {
     if (D == 64)
       return pf ? dispatch_attn<__half, 64, true>(BM, BN, Q, K, V, O, B, H, S, SQO, SKV, st, o)
@@ -241,6 +253,43 @@ const char* attn_error_string(int code) {
     case ATTN_ERR_SHARD: return "invalid multi-GPU partition";
     default: return "unknown error";
   }
+}
+
+int attn_set_split(int mode) {
+  if (mode < 0 || mode > kMaxSplit) return ATTN_ERR_INVALID_ARG;
+  g_split_mode.store(mode);
+  return ATTN_OK;
+}
+
+int attn_plan_split(long long units, int num_kv_tiles, long long slots, int mode, int* split,
+                    long long* whole_units, long long* ctas) {
+  if (units < 0 || num_kv_tiles < 0 || slots <= 0 || mode < 0 || mode > kMaxSplit)
+    return ATTN_ERR_INVALID_ARG;
+  const SplitPlan pl = plan_split(units, num_kv_tiles, slots, mode);
+  if (split) *split = pl.split;
+  if (whole_units) *whole_units = pl.whole;
+  if (ctas) *ctas = pl.ctas;
+  return ATTN_OK;
+}
+
+int attn_query_split(int B, int H, int S, int D, int dtype, int BM, int BN, int* split,
+                     long long* whole_units, long long* ctas, unsigned long long* workspace_bytes) {
+  if (B < 0 || H < 0 || S < 0) return ATTN_ERR_INVALID_ARG;
+  if (dtype != ATTN_DTYPE_F16 && dtype != ATTN_DTYPE_BF16) return ATTN_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128) return ATTN_ERR_UNSUPPORTED;
+  SplitPlan pl;
+  LaunchOpts o;
+  o.split = g_split_mode.load();
+  o.plan_out = &pl;
+  o.plan_only = true;
+  const int rc = dispatch(nullptr, nullptr, nullptr, nullptr, B, H, S, D, S, S, dtype, BM, BN,
+                          nullptr, o);
+  if (rc != ATTN_OK) return rc;
+  if (split) *split = pl.split;
+  if (whole_units) *whole_units = pl.whole;
+  if (ctas) *ctas = pl.ctas;
+  if (workspace_bytes) *workspace_bytes = pl.ws_bytes;
+  return ATTN_OK;
 }
 
 int attn_debug_fault(int mode) {

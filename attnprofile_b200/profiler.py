@@ -37,12 +37,17 @@ PHASES = ["LoadQ", "LoadK", "LoadV", "GEMM-QK", "SOFTMAX", "GEMM-PV"]
 # decision, exponentials with the P tcgen05.st issued, wait for the P stores.
 SUBPHASES = ["S-ld", "max", "exp", "P-st"]
 ALL_PHASES = PHASES + SUBPHASES
+# The epilogue phase (index 10) is stamped once per CTA; its slots are steps:
+# the whole epilogue, the wait for the last P V, the partial-O write and the
+# count-in of a split part, the merge (split) or O normalisation (whole), and
+# the TMA store issue.
+EPILOGUE_STEPS = ["epilogue", "ep-waitO", "ep-partial", "ep-count", "ep-merge", "ep-store"]
 
 
 def summarize(stamps_list) -> dict:
     """Mean cycles per phase over recorded slots and runs.
 
-    stamps_list: iterable of int64 arrays [6, 32, 2] (begin, end); 0 = unset."""
+    stamps_list: iterable of int64 arrays [phases, 32, 2] (begin, end); 0 = unset."""
     import numpy as np
     sums = {p: [] for p in ALL_PHASES}
     periods = []
@@ -60,6 +65,17 @@ def summarize(stamps_list) -> dict:
             periods.extend(np.diff(sb[1:]).tolist())  # skip the first (pipeline fill)
     out = {p: (float(np.mean(v)) if v else float("nan")) for p, v in sums.items()}
     out["period"] = float(np.mean(periods)) if periods else float("nan")
+    ep = {n: [] for n in EPILOGUE_STEPS}
+    for st in stamps_list:
+        a = np.asarray(st, dtype=np.int64)
+        if a.shape[0] <= len(ALL_PHASES):
+            continue
+        for k, n in enumerate(EPILOGUE_STEPS):
+            b, e = a[len(ALL_PHASES), k]
+            if b != 0 and e != 0 and e >= b:
+                ep[n].append(int(e - b))
+    for n, v in ep.items():
+        out[n] = float(np.mean(v)) if v else float("nan")
     return out
 
 

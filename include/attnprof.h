@@ -66,12 +66,15 @@ int attn_fwd_padded(const void* Q, const void* K, const void* V, void* O, int B,
 
 /*
  * attn_fwd_profiled -- attn_fwd with the per-phase cycle profiler compiled in
- * (f16 and bf16).  CTA number profile_cta (blockIdx.y * gridDim.x + blockIdx.x)
- * writes clock64 begin/end stamps for the phases LoadQ, LoadK, LoadV, GEMM-QK,
+ * (f16 and bf16).  CTA number profile_cta (CTAs are numbered in launch
+ * order; CTA 0 runs the first BM query rows of head 0 over all keys) writes
+ * clock64 begin/end stamps for the phases LoadQ, LoadK, LoadV, GEMM-QK,
  * SOFTMAX, GEMM-PV (then the SOFTMAX steps S-load, max, exp, P-store) of its
- * first 32 KV iterations into dev_profile_buf, laid out as u64 [10][32][2]
- * (see attn_profile_layout).  The caller zeroes the
- * buffer before the launch; unstamped slots stay 0.
+ * first 32 KV iterations, and for its epilogue (phase 10; slots 0-5: the
+ * whole epilogue, the wait for the last P V, partial-O write and count-in of
+ * a split part, merge or O normalisation, O store issue), into
+ * dev_profile_buf, laid out as u64 [11][32][2] (see attn_profile_layout).
+ * The caller zeroes the buffer before the launch; unstamped slots stay 0.
  * Replaces: the clock64 profiler of attn.cu (ProfileResult attn.cu:5-22,
  *           stamps attn.cu:133-444, run_one_case attn.cu:1400-1494).
  */
@@ -79,7 +82,7 @@ int attn_fwd_profiled(const void* Q, const void* K, const void* V, void* O, int 
                       int D, int dtype, int BM, int BN, void* stream,
                       unsigned long long* dev_profile_buf, int profile_cta);
 
-/* Profile buffer geometry: *phases = 10, *slots = 32 (u64 pairs). */
+/* Profile buffer geometry: *phases = 11, *slots = 32 (u64 pairs). */
 int attn_profile_layout(int* phases, int* slots);
 
 /*
@@ -122,6 +125,32 @@ void attn_set_timeout_ns(unsigned long long ns);
  */
 int attn_query_config(int D, int BM, int BN, int dtype, int* num_threads, int* smem_bytes,
                       int* tmem_cols, int* stages);
+
+/*
+ * Key split of the last wave.  A launch has U = B*H*ceil(S/BM) units (BM
+ * query rows of one head); a B200 runs one unit per SM at a time, so when U
+ * is not a multiple of the SM count the last wave leaves SMs idle (1x16x4096
+ * at BM=256: 256 units on 148 SMs).  Each unit of that last wave can instead
+ * run as k CTAs over disjoint key ranges; every part writes its normalised
+ * partial O and (row max, row sum) to a stream-ordered workspace, and the
+ * part that finishes last merges them (fixed order: the result does not
+ * depend on arrival order).  Default: automatic (a cost model picks k).
+ *
+ * attn_set_split -- mode 0 automatic, 1 never split, 2..4 force k-way splits
+ *   of the last wave (of the last full wave when U is a multiple of the slot
+ *   count) for kernels launched after this call.
+ * attn_plan_split -- the planner alone (host only, no GPU): U units,
+ *   num_kv_tiles = ceil(S/BN), `slots` resident CTAs per wave.
+ * attn_query_split -- the plan and workspace size for a problem on the
+ *   current device (needs a GPU).
+ * No counterpart in the reference, whose grid is one CTA per unit
+ * (tuning/attn_test.cu:1583-1663).
+ */
+int attn_set_split(int mode);
+int attn_plan_split(long long units, int num_kv_tiles, long long slots, int mode, int* split,
+                    long long* whole_units, long long* ctas);
+int attn_query_split(int B, int H, int S, int D, int dtype, int BM, int BN, int* split,
+                     long long* whole_units, long long* ctas, unsigned long long* workspace_bytes);
 
 /* Human-readable text for a return code.  Never NULL. */
 const char* attn_error_string(int code);

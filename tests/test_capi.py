@@ -105,3 +105,51 @@ def test_no_cpu_fallback_without_gpu(engine):
     good = 0x10000
     rc = engine.lib().attn_fwd(good, good, good, good, 1, 1, 64, 128, 0, 128, 128, None)
     assert rc == engine.ERR["CUDA"]
+
+
+def test_plan_split_cost_model(engine):
+    # Few long units leave most SMs idle: 1x1x16384 at BM=256, BN=128 has
+    # 64 units of 128 key tiles; two key ranges each fill 128 SMs.
+    assert engine.plan_split(64, 128, 148) == {"split": 2, "whole": 0, "ctas": 128}
+    # 1x6x8192: 192 units of 64 tiles; the 44 of the second wave run as 3 ranges.
+    assert engine.plan_split(192, 64, 148) == {"split": 3, "whole": 148, "ctas": 148 + 44 * 3}
+    # A second wave of many units (1x16x4096: 256 units of 32 tiles) does not
+    # pay for the partial-O write and merge: unsplit.
+    assert engine.plan_split(256, 32, 148)["split"] == 1
+    # Short units do not either (1x16x1024: 64 units of 8 tiles).
+    assert engine.plan_split(64, 8, 148)["split"] == 1
+    # Units that fill whole waves (8x32x8192 and 1x64x32768 at BM=256 give
+    # 8192 units; 8192 % 148 = 52, a short tail of a long run) stay unsplit.
+    assert engine.plan_split(8192, 64, 148)["split"] == 1
+    assert engine.plan_split(296, 32, 148)["split"] == 1     # exactly two waves
+
+
+@pytest.mark.parametrize("units,n_kv,slots", [(256, 32, 148), (17, 8, 16), (3, 2, 148),
+                                              (1000, 5, 148), (148, 64, 148), (0, 8, 148)])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3, 4])
+def test_plan_split_invariants(engine, units, n_kv, slots, mode):
+    p = engine.plan_split(units, n_kv, slots, mode)
+    k = p["split"]
+    assert 1 <= k <= min(4, max(n_kv, 1))
+    assert 0 <= p["whole"] <= units
+    assert p["ctas"] == p["whole"] + (units - p["whole"]) * k
+    if mode == 1 or units == 0:
+        assert k == 1 and p["whole"] == units
+    if k > 1:
+        assert k <= n_kv                 # every key range holds at least one tile
+    if mode >= 2 and units and n_kv >= 2:
+        assert k == min(mode, n_kv)      # forced split
+    if k == 1:
+        assert p["whole"] == units
+
+
+def test_plan_split_rejects_bad_arguments(engine):
+    L = engine.lib()
+    k, w, c = ctypes.c_int(), ctypes.c_longlong(), ctypes.c_longlong()
+    args = (ctypes.byref(k), ctypes.byref(w), ctypes.byref(c))
+    assert L.attn_plan_split(10, 4, 0, 0, *args) == engine.ERR["INVALID_ARG"]
+    assert L.attn_plan_split(10, 4, 148, 5, *args) == engine.ERR["INVALID_ARG"]
+    assert L.attn_plan_split(-1, 4, 148, 0, *args) == engine.ERR["INVALID_ARG"]
+    assert L.attn_set_split(5) == engine.ERR["INVALID_ARG"]
+    assert L.attn_set_split(-1) == engine.ERR["INVALID_ARG"]
+    assert L.attn_set_split(0) == 0
