@@ -22,7 +22,7 @@ __all__ = [
 
 ERR = {
     "OK": 0, "INVALID_ARG": -1, "UNSUPPORTED": -2, "MISALIGNED": -3, "CUDA": -4,
-    "TENSOR_MAP": -5, "DEVICE_TIMEOUT": -6, "RESOURCE": -7, "SHARD": -8,
+    "TENSOR_MAP": -5, "DEVICE_TIMEOUT": -6, "RESOURCE": -7, "SHARD": -8, "SCRATCH_LIMIT": -9,
 }
 DTYPE_F16 = 0
 DTYPE_BF16 = 1

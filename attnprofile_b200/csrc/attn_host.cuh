@@ -66,6 +66,7 @@ struct LaunchOpts {
   size_t workspace_bytes = 0;
   SplitPlan* plan_out = nullptr; // receives the plan
   bool plan_only = false;        // compute the plan, launch nothing
+  bool cache_maps = true;        // false: encode tensor maps per call, no host allocation
 };
 
 // Chooses the key split of the last, partially filled wave of units.  A
@@ -195,12 +196,14 @@ struct MapKeyHash {
 // 3-D map over a [B*H][rows][D] tensor: dims {D, S, B*H}; the row pitch is D
 // elements and the head pitch `rows` rows, so rows >= S padding is skipped.
 // Box {64, box_rows, 1} with 128-byte swizzle: one 64-column block per copy.
+// use_cache = false encodes the map without touching the cache (no host
+// allocation).
 inline int get_tensor_map(CUtensorMap* out, const void* ptr, int dtype, int D, int S, int BH,
-                          long long rows, int box_rows) {
+                          long long rows, int box_rows, bool use_cache = true) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
   const MapKey key{reinterpret_cast<uintptr_t>(ptr), dtype, D, S, BH, box_rows, rows};
-  {
+  if (use_cache) {
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {
@@ -223,7 +226,7 @@ inline int get_tensor_map(CUtensorMap* out, const void* ptr, int dtype, int D, i
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return ATTN_ERR_TENSOR_MAP;
-  {
+  if (use_cache) {
     std::lock_guard<std::mutex> g(mu);
     if (cache.size() > 4096) cache.clear();
     cache.emplace(key, m);
@@ -272,10 +275,11 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
 
   CUtensorMap mq, mk, mv, mo;
   int rc;
-  if ((rc = get_tensor_map(&mq, Q, dtype, D, S, static_cast<int>(BH), q_rows, C::QROWS))) return rc;
-  if ((rc = get_tensor_map(&mk, K, dtype, D, S, static_cast<int>(BH), kv_rows, BN))) return rc;
-  if ((rc = get_tensor_map(&mv, V, dtype, D, S, static_cast<int>(BH), kv_rows, BN))) return rc;
-  if ((rc = get_tensor_map(&mo, O, dtype, D, S, static_cast<int>(BH), q_rows, C::QROWS))) return rc;
+  const int bhi = static_cast<int>(BH);
+  if ((rc = get_tensor_map(&mq, Q, dtype, D, S, bhi, q_rows, C::QROWS, o.cache_maps))) return rc;
+  if ((rc = get_tensor_map(&mk, K, dtype, D, S, bhi, kv_rows, BN, o.cache_maps))) return rc;
+  if ((rc = get_tensor_map(&mv, V, dtype, D, S, bhi, kv_rows, BN, o.cache_maps))) return rc;
+  if ((rc = get_tensor_map(&mo, O, dtype, D, S, bhi, q_rows, C::QROWS, o.cache_maps))) return rc;
 
   AttnParams p;
   p.S = S;

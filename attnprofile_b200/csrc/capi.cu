@@ -93,6 +93,26 @@ static int dispatch(const void* Q, const void* K, const void* V, void* O, int B,
             : dispatch_attn<__nv_bfloat16, 128, false>(BM, BN, Q, K, V, O, B, H, S, SQO, SKV, st, o);
 }
 
+// Launch with a caller-provided workspace and per-call tensor maps (no
+// device or host allocation); the other settings as for attn_fwd.  When
+// plan_only is set, only *plan is filled.  Used by attn_fwd_noalloc.
+int run_in_workspace(const void* Q, const void* K, const void* V, void* O, int B, int H, int S,
+                     int D, int dtype, int BM, int BN, cudaStream_t st, void* ws,
+                     size_t ws_bytes, SplitPlan* plan, bool plan_only) {
+  const int v = validate(Q, K, V, O, B, H, S, D, S, S, dtype);
+  if (v <= 0) return v;
+  LaunchOpts o;
+  o.timeout_ns = g_timeout_ns.load();
+  o.fault_mode = g_fault_mode.load();
+  o.split = g_split_mode.load();
+  o.workspace = ws;
+  o.workspace_bytes = ws_bytes;
+  o.plan_out = plan;
+  o.plan_only = plan_only;
+  o.cache_maps = false;
+  return dispatch(Q, K, V, O, B, H, S, D, S, S, dtype, BM, BN, st, o);
+}
+
 }  // namespace attnprof
 
 using namespace attnprof;
@@ -251,6 +271,9 @@ const char* attn_error_string(int code) {
     case ATTN_ERR_DEVICE_TIMEOUT: return "bounded in-kernel wait expired (device timeout)";
     case ATTN_ERR_RESOURCE: return "shared memory or tensor memory request over the limit";
     case ATTN_ERR_SHARD: return "invalid multi-GPU partition";
+    case ATTN_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the fixed no-allocation buffer holds "
+             "(ATTN_NOALLOC_SCRATCH_BYTES); use attn_fwd";
     default: return "unknown error";
   }
 }

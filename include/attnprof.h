@@ -39,6 +39,7 @@ extern "C" {
 #define ATTN_ERR_DEVICE_TIMEOUT -6 /* a bounded in-kernel wait expired              */
 #define ATTN_ERR_RESOURCE -7       /* shared memory / TMEM request over the limit   */
 #define ATTN_ERR_SHARD -8          /* multi-GPU partition error                     */
+#define ATTN_ERR_SCRATCH_LIMIT -9  /* attn_fwd_noalloc: scratch over its fixed size  */
 
 /*
  * attn_fwd -- one attention forward over contiguous [B, H, S, D] tensors.
@@ -151,6 +152,31 @@ int attn_plan_split(long long units, int num_kv_tiles, long long slots, int mode
                     long long* whole_units, long long* ctas);
 int attn_query_split(int B, int H, int S, int D, int dtype, int BM, int BN, int* split,
                      long long* whole_units, long long* ctas, unsigned long long* workspace_bytes);
+
+/*
+ * attn_fwd_noalloc -- attn_fwd for callers that must not allocate GPU
+ * memory: code running inside a CUDA graph being captured, a host thread that
+ * holds a preallocated memory budget, or an allocator callback.  Arguments
+ * and results are those of attn_fwd.  When the launch's plan splits units
+ * along the keys (attn_set_split / attn_query_split) it needs scratch for the
+ * partial results; attn_fwd takes that from a stream-ordered pool, this entry
+ * point from a fixed array of ATTN_NOALLOC_SCRATCH_BYTES that the library
+ * holds in every GPU's memory from the first call on that GPU until the
+ * process exits.  It calls no cudaMalloc / cudaFree / pool allocation, and
+ * encodes its tensor maps per call instead of caching them.
+ *   - A plan needing more scratch returns ATTN_ERR_SCRATCH_LIMIT and launches
+ *     nothing (attn_fwd runs any size).
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls share the one array.  Calls that may overlap on the GPU
+ *     (different streams, or different host threads) race on it; order them
+ *     on one stream.  Each call clears the counters it needs at zero.
+ * No counterpart in the reference: its launchers allocate nothing beyond
+ * the caller's tensors (tuning/attn_test.cu:1583-1663) and have no key split.
+ */
+#define ATTN_NOALLOC_SCRATCH_BYTES (32u << 20)
+int attn_fwd_noalloc(const void* Q, const void* K, const void* V, void* O, int B, int H, int S,
+                     int D, int dtype, int BM, int BN, void* stream);
 
 /* Human-readable text for a return code.  Never NULL. */
 const char* attn_error_string(int code);
