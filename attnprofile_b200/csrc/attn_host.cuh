@@ -36,12 +36,17 @@ namespace attnprof {
 
 constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per CTA on sm_100
 
+// Deepest K/V ring (at most `cap` slots) that fits the shared memory of one
+// CTA, or of each of two CTAs on an SM for the variants built for two
+// (AttnConfig::MIN_CTAS_PER_SM; the SM has 233472 bytes, 1 KB of which each
+// CTA reserves).
 template <typename T, int D, int BN, int NQ>
 constexpr int auto_stages(int cap = 8) {
+  using C2 = AttnConfig<T, D, BN, NQ, 2>;
+  const int limit = C2::MIN_CTAS_PER_SM == 2 ? 233472 / 2 - 1024 : kSmemLimit;
   int best = 0;
   for (int s = 2; s <= cap; ++s) {
-    if (AttnConfig<T, D, BN, NQ, 2>::OFF_KV + s * (BN * D * 2) + 256 + 1024 + 16 <= kSmemLimit)
-      best = s;
+    if (C2::OFF_KV + s * (BN * D * 2) + 256 + 1024 + 16 <= limit) best = s;
   }
   return best;
 }
