@@ -235,8 +235,8 @@ struct AttnConfig {
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
 // Of every 8 (column-pair) exponentials in a softmax chunk, this many run as
-// the FMA-pipe polynomial (ptx::exp2_poly) and the rest on the MUFU unit, so
-// the two pipes share the B*H*S^2 exponentials.
+// the FMA-pipe polynomial (ptx::exp2_poly_pair) and the rest on the MUFU
+// unit, so the two pipes share the B*H*S^2 exponentials.
 #ifndef ATTNPROF_POLY_PAIRS_OF_8
 #define ATTNPROF_POLY_PAIRS_OF_8 0
 #endif
@@ -613,6 +613,7 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
     const float neg = -m_run * sl2;
     const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
     const uint64_t negx2 = ptx::f2_pack(neg, neg);
+    const float poly_a = sl2 * (1.0f / 134.0f), poly_b = (neg + 126.0f) * (1.0f / 134.0f);
     uint64_t part[2] = {0ull, 0ull};  // packed partial row sums (4 short FADD chains)
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
@@ -630,15 +631,16 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int c0 = (KEEP ? c * 32 : 0) + 2 * e;
-        // x = s * scale_log2 - m * scale_log2 for two columns in one f32x2 FMA
-        const uint64_t x2 = ptx::f2_fma(
-            ptx::f2_pack(__uint_as_float(sreg[c0]), __uint_as_float(sreg[c0 + 1])), sl2x2, negx2);
-        float x0, x1;
-        ptx::f2_unpack(x2, x0, x1);
         float p0, p1;
         if (poly_pair(e)) {
-          ptx::exp2_poly_x2(x0, x1, p0, p1);
+          ptx::exp2_poly_pair(__uint_as_float(sreg[c0]), __uint_as_float(sreg[c0 + 1]), poly_a,
+                              poly_b, p0, p1);
         } else {
+          // x = s * scale_log2 - m * scale_log2 for two columns in one f32x2 FMA
+          const uint64_t x2 = ptx::f2_fma(
+              ptx::f2_pack(__uint_as_float(sreg[c0]), __uint_as_float(sreg[c0 + 1])), sl2x2, negx2);
+          float x0, x1;
+          ptx::f2_unpack(x2, x0, x1);
           p0 = ptx::ex2_approx(x0);
           p1 = ptx::ex2_approx(x1);
         }

@@ -310,25 +310,6 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return d;
 }
 
-// exp2_poly for a pair of arguments, the FMA work done in f32x2 (two lanes per
-// instruction): same range reduction and polynomial as exp2_poly.
-__device__ __forceinline__ void exp2_poly_x2(float x0, float x1, float& p0, float& p1) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  const uint64_t xc = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
-  const uint64_t t = f2_add(xc, f2_pack(kRound, kRound));
-  const uint64_t j = f2_add(t, f2_pack(-kRound, -kRound));
-  const uint64_t f = f2_fma(j, f2_pack(-1.0f, -1.0f), xc);
-  uint64_t p = f2_fma(f2_pack(0.05517132207751274f, 0.05517132207751274f), f,
-                      f2_pack(0.24261054396629333f, 0.24261054396629333f));
-  p = f2_fma(p, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
-  p = f2_fma(p, f, f2_pack(0.9999281167984009f, 0.9999281167984009f));
-  float q0, q1, t0, t1;
-  f2_unpack(p, q0, q1);
-  f2_unpack(t, t0, t1);
-  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
-  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
-}
-
 // Three-input maximum (sm_100 max.f32 with three sources).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
@@ -336,27 +317,44 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// exp2 on the FMA pipe, for the share of elements taken off the MUFU unit.
-// Range reduction 2^x = 2^j * 2^f with j = round(x), f = x - j in [-1/2, 1/2]:
-// adding 1.5 * 2^23 rounds x to an integer held in the low mantissa bits, and
-// 2^j is applied by adding j to the exponent field of 2^f.  2^f is a degree-3
-// polynomial fitted here to minimise the relative error on [-1/2, 1/2]
-// (Lawson's iteratively reweighted least squares); max relative error of the
-// float32 evaluation 7.5e-5, below the 4.9e-4 half-ulp of the f16 P it feeds.
-// x is clamped to >= -125 so the exponent field never underflows; 2^-125 is
-// zero after rounding to f16 and negligible (< 3e-38) in bf16.
-__device__ __forceinline__ float exp2_poly(float x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c0 = 0.9999281167984009f, c1 = 0.6932609677314758f;
-  constexpr float c2 = 0.24261054396629333f, c3 = 0.05517132207751274f;
-  x = fmaxf(x, -125.0f);
-  const float t = __fadd_rn(x, kRound);
-  const float j = __fsub_rn(t, kRound);
-  const float f = __fsub_rn(x, j);
-  float p = fmaf(c3, f, c2);
-  p = fmaf(p, f, c1);
-  p = fmaf(p, f, c0);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// exp2 on the FMA pipe, for the share of elements taken off the MUFU unit,
+// for two scores at once: p = 2^x with x = s * sl2 + neg, given
+// a = sl2 / 134 and b = (neg + 126) / 134.
+//  * clamp: y = sat(s * a + b) = (clamp(x, -126, 8) + 126) / 134, one
+//    saturating FMA per score (x = -inf from masked keys gives y = 0);
+//  * range reduction 2^x = 2^j * 2^f with j = round(x), f = x - j in
+//    [-1/2, 1/2]: t = 134 y + (1.5 * 2^23 - 126) holds j in its low mantissa
+//    bits (the magic-number rounding of 1.5 * 2^23), u = t - (1.5 * 2^23 -
+//    126) = j + 126 exactly, f = 134 y - u;
+//  * 2^f by a degree-3 polynomial fitted here to minimise the relative error
+//    on [-1/2, 1/2] (Lawson's iteratively reweighted least squares), max
+//    relative error of the float32 evaluation 7.5e-5, below the 4.9e-4
+//    half-ulp of the f16 P it feeds;
+//  * 2^j applied by adding j << 23 to the bits of 2^f: (t_bits << 23) mod 2^32
+//    is j << 23, so one integer multiply-add t_bits * 2^23 + bits(2^f).
+//    j >= -126 keeps the exponent field from wrapping.
+// Everything runs on the FMA pipe (f32x2 where it exists), no MUFU, no ALU.
+__device__ __forceinline__ void exp2_poly_pair(float s0, float s1, float a, float b, float& p0,
+                                               float& p1) {
+  constexpr float kR = 134.0f, kMagic = 12582912.0f - 126.0f;
+  float y0, y1;
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(y0) : "f"(s0), "f"(a), "f"(b));
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(y1) : "f"(s1), "f"(a), "f"(b));
+  const uint64_t y = f2_pack(y0, y1);
+  const uint64_t t = f2_fma(y, f2_pack(kR, kR), f2_pack(kMagic, kMagic));
+  const uint64_t u = f2_add(t, f2_pack(-kMagic, -kMagic));
+  float u0, u1;
+  f2_unpack(u, u0, u1);
+  const uint64_t f = f2_fma(y, f2_pack(kR, kR), f2_pack(-u0, -u1));
+  uint64_t p = f2_fma(f2_pack(0.05517132207751274f, 0.05517132207751274f), f,
+                      f2_pack(0.24261054396629333f, 0.24261054396629333f));
+  p = f2_fma(p, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  p = f2_fma(p, f, f2_pack(0.9999281167984009f, 0.9999281167984009f));
+  float q0, q1, t0, t1;
+  f2_unpack(p, q0, q1);
+  f2_unpack(t, t0, t1);
+  p0 = __uint_as_float(__float_as_uint(t0) * 8388608u + __float_as_uint(q0));
+  p1 = __uint_as_float(__float_as_uint(t1) * 8388608u + __float_as_uint(q1));
 }
 
 }  // namespace ptx
