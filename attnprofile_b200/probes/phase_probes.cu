@@ -1,0 +1,398 @@
+// Phase-isolation probes for the B200 attention kernel: each phase of one KV
+// iteration run alone, one CTA per SM, so the per-phase profile of the full
+// kernel (profiler.py) can be read against what each phase costs in
+// isolation.  The B200 counterparts of the reference's TMA-only streaming
+// probe (tma_ws.cu:26-298) and MMA-only probe (attn.cu:502-900,
+// gemm_ws.cu:63-216), plus a softmax-only probe:
+//
+//   tma      K/V tiles (BN x D, f16, 128B swizzle) streamed through a STAGES
+//            ring by a TMA producer warp; a consumer warp releases each slot as
+//            soon as it lands.  -> cycles per K+V tile pair, GB/s per SM.
+//   mma      the MMA warp's issue sequence for one KV iteration of a
+//            two-Q-tile CTA (P V then S = Q K^T for each tile; SS and TS
+//            tcgen05.mma, 128 x 128 x 16 each) on resident operands, in
+//            several orders and with one or two issuing warps.
+//            -> cycles per iteration vs the 2048-cycle tensor work.
+//   softmax  the softmax step of one 128 x BN tile per warpgroup (tcgen05.ld
+//            of S, row max, exp2 on MUFU, P packed to f16 and tcgen05.st back),
+//            one or two warpgroups.  -> cycles per tile per warpgroup.
+//
+// Every wait is bounded (globaltimer, 2 s); a probe that times out reports
+// it and the program exits non-zero.  Operands are zero-filled or synthetic:
+// the probes measure time, not results.
+//
+// Usage: phase_probes [tma|mma|softmax|all]
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../csrc/attn_kernel.cuh"  // ptx wrappers, row_max
+
+using namespace attnprof;
+
+namespace {
+
+constexpr unsigned long long kTimeoutNs = 2000000000ull;
+__device__ int g_probe_timeout;
+
+__device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = ptx::globaltimer_ns();
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (ptx::globaltimer_ns() - t0 > kTimeoutNs) {
+      atomicExch(&g_probe_timeout, 1);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// tma: K/V streaming through the ring
+// ---------------------------------------------------------------------------
+constexpr int D = 128, BN = 128;
+constexpr int TILE_BYTES = BN * D * 2;
+
+template <int STAGES>
+__global__ void __launch_bounds__(64, 1)
+    tma_probe(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+              int heads, int n_tiles, unsigned long long* cycles) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&empty[s]), 1);
+    }
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  const int head = blockIdx.x % heads;
+  const int items = 2 * n_tiles;  // K_j, V_j
+  const unsigned long long t0 = clock64();
+  if (warp == 0 && lane == 0) {
+    for (int t = 0; t < items; ++t) {
+      const int s = t % STAGES, r = t / STAGES;
+      if (r > 0 && !bounded_wait(ptx::smem_u32(&empty[s]), (r - 1) & 1)) break;
+      const uint32_t bar = ptx::smem_u32(&full[s]);
+      ptx::mbar_arrive_expect_tx(bar, TILE_BYTES);
+      const CUtensorMap* m = (t & 1) ? &tmV : &tmK;
+      for (int d = 0; d < D / 64; ++d)
+        ptx::tma_load_3d(base + s * TILE_BYTES + d * BN * 128, m, bar, d * 64, (t / 2) * BN, head);
+    }
+  } else if (warp == 1 && lane == 0) {
+    for (int t = 0; t < items; ++t) {
+      const int s = t % STAGES;
+      if (!bounded_wait(ptx::smem_u32(&full[s]), (t / STAGES) & 1)) break;
+      ptx::mbar_arrive(ptx::smem_u32(&empty[s]));
+    }
+    cycles[blockIdx.x] = clock64() - t0;
+  }
+  __syncthreads();
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+bool make_map(CUtensorMap* m, void* ptr, int heads, int S) {
+  static EncodeFn enc = nullptr;
+  if (!enc) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess)
+      return false;
+    enc = reinterpret_cast<EncodeFn>(p);
+  }
+  const cuuint64_t dims[3] = {D, static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(heads)};
+  const cuuint64_t strides[2] = {D * 2, static_cast<cuuint64_t>(S) * D * 2};
+  const cuuint32_t box[3] = {64, BN, 1}, es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ptr, dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------------------
+// mma: one KV iteration of a two-Q-tile CTA on resident operands
+// ---------------------------------------------------------------------------
+// TMEM: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512); P_i over the
+// first 64 columns of S_i.  smem: Q0, Q1 (128 x 128 f16 each), K, V tiles.
+constexpr int MMA_SMEM = 4 * 32768 + 1024;
+enum MmaOrder : int {
+  kKernelOrder = 0,  // PV0, S0, PV1, S1 by one issuer (the kernel's order)
+  kTwoIssuers = 1,   // tile 0 by warp 0, tile 1 by warp 1 (PV_i, S_i each)
+  kGrouped = 2,      // PV0, PV1, S0, S1 by one issuer
+  kQkOnly = 3,       // S0, S1
+  kPvOnly = 4,       // PV0, PV1
+};
+
+__global__ void __launch_bounds__(128, 1) mma_probe(int order, int iters, unsigned long long* cycles) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - ptx::smem_u32(smem_raw));
+  __shared__ uint32_t tmem_slot;
+  __shared__ __align__(8) uint64_t done[2];
+  const int warp = threadIdx.x / 32;
+  for (int i = threadIdx.x; i < 4 * 32768 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(g)[i] = 0;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(&done[0]), 1);
+    ptx::mbar_init(ptx::smem_u32(&done[1]), 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_u32(&tmem_slot), 512);
+    ptx::tmem_relinquish();
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t q0 = base, k = base + 2 * 32768, v = base + 3 * 32768;
+  const uint32_t id_s = ptx::idesc_f16(128, 128, false, false);
+  const uint32_t id_pv = ptx::idesc_f16(128, 128, false, true);
+  auto qk = [&](int i) {
+    const uint64_t qd = ptx::smem_desc_sw128(q0 + i * 32768, 16, 1024);
+    const uint64_t kd = ptx::smem_desc_sw128(k, 16, 1024);
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+      ptx::mma_ss(tmem + i * 128, qd + off, kd + off, id_s, kk > 0 ? 1u : 0u);
+    }
+  };
+  auto pv = [&](int i) {
+    const uint64_t vd = ptx::smem_desc_sw128(v, 128 * 128, 1024);
+    for (int kk = 0; kk < 8; ++kk)
+      ptx::mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
+                  vd + static_cast<uint64_t>(kk * 2048 >> 4), id_pv, 1u);
+  };
+  const bool two = order == kTwoIssuers;
+  const int my_tile = warp;  // for two issuers
+  if (threadIdx.x % 32 == 0 && (warp == 0 || (two && warp == 1))) {
+    const unsigned long long t0 = clock64();
+    for (int it = 0; it < iters; ++it) {
+      if (two) {
+        pv(my_tile);
+        qk(my_tile);
+      } else if (order == kKernelOrder) {
+        pv(0); qk(0); pv(1); qk(1);
+      } else if (order == kGrouped) {
+        pv(0); pv(1); qk(0); qk(1);
+      } else if (order == kQkOnly) {
+        qk(0); qk(1);
+      } else {
+        pv(0); pv(1);
+      }
+    }
+    const uint32_t bar = ptx::smem_u32(&done[two ? my_tile : 0]);
+    ptx::mma_commit(bar);
+    bounded_wait(bar, 0);
+    cycles[blockIdx.x * 2 + (two ? my_tile : 0)] = clock64() - t0;
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// softmax: one 128 x BN softmax step per warpgroup
+// ---------------------------------------------------------------------------
+template <int NWG>
+__global__ void __launch_bounds__(128 * NWG, 1) softmax_probe(int iters, unsigned long long* cycles,
+                                                             float* sink) {
+  __shared__ uint32_t tmem_slot;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int wg = warp / 4, wi = warp & 3;
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_u32(&tmem_slot), 256);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(wi * 32) << 16);
+  const uint32_t s_col = wg * BN;
+  // synthetic S row: N(0,1)-like spread of scores
+  {
+    uint32_t r[32];
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        r[e] = __float_as_uint(0.37f * (((threadIdx.x * 131 + c * 32 + e) * 2654435761u >> 20) % 19) - 3.3f);
+      ptx::tmem_st32(lane_base + s_col + c * 32, r);
+    }
+    ptx::tmem_wait_st();
+  }
+  const float sl2 = 0.12752f;
+  float m_run = -INFINITY, l_run = 0.f;
+  __syncthreads();
+  const unsigned long long t0 = clock64();
+#pragma unroll 1
+  for (int it = 0; it < iters; ++it) {
+    uint32_t s[BN];
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t(&r)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]);
+      ptx::tmem_ld32(lane_base + s_col + c * 32, r);
+    }
+    ptx::tmem_wait_ld();
+    ptx::reg_fence(s);
+    const float m_new = row_max<BN>(s, m_run);
+    const float alpha = ptx::ex2_approx((m_run - m_new) * sl2);
+    m_run = m_new;
+    const float neg = -m_new * sl2;
+    const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2), negx2 = ptx::f2_pack(neg, neg);
+    uint64_t part[2] = {0ull, 0ull};
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int c0 = c * 32 + 2 * e;
+        const uint64_t x2 = ptx::f2_fma(ptx::f2_pack(__uint_as_float(s[c0]), __uint_as_float(s[c0 + 1])),
+                                        sl2x2, negx2);
+        float x0, x1;
+        ptx::f2_unpack(x2, x0, x1);
+        const float p0 = ptx::ex2_approx(x0), p1 = ptx::ex2_approx(x1);
+        part[e & 1] = ptx::f2_add(part[e & 1], ptx::f2_pack(p0, p1));
+        __half2 h = __floats2half2_rn(p0, p1);
+        pk[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      // P over the first half of the S columns, as the kernel stores it (the
+      // next iteration reloads the same S region: the probe keeps the data
+      // path, not the values)
+      ptx::tmem_st16(lane_base + s_col + c * 16, pk);
+    }
+    ptx::tmem_wait_st();
+    float a, b, c, d;
+    ptx::f2_unpack(part[0], a, b);
+    ptx::f2_unpack(part[1], c, d);
+    l_run = l_run * alpha + ((a + b) + (c + d));
+  }
+  const unsigned long long t1 = clock64();
+  if (lane == 0 && wi == 0) cycles[blockIdx.x * 2 + wg] = t1 - t0;
+  sink[blockIdx.x * blockDim.x + threadIdx.x] = l_run;
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 256);
+  }
+}
+
+double mean_of(const std::vector<unsigned long long>& v, int stride, int off, int n) {
+  double s = 0;
+  int k = 0;
+  for (int i = 0; i < n; ++i) {
+    if (v[i * stride + off]) {
+      s += static_cast<double>(v[i * stride + off]);
+      ++k;
+    }
+  }
+  return k ? s / k : 0.0;
+}
+
+bool check(const char* what) {
+  const cudaError_t e = cudaDeviceSynchronize();
+  int to = 0;
+  cudaMemcpyFromSymbol(&to, g_probe_timeout, sizeof(int));
+  if (e != cudaSuccess || to) {
+    std::printf("%s: %s%s\n", what, cudaGetErrorString(e), to ? " (bounded wait expired)" : "");
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  const char* which = argc > 1 ? argv[1] : "all";
+  const bool all = !std::strcmp(which, "all");
+  int sms = 0, clk_khz = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  cudaDeviceGetAttribute(&clk_khz, cudaDevAttrClockRate, 0);
+  unsigned long long* cyc = nullptr;
+  float* sink = nullptr;
+  cudaMalloc(&cyc, sizeof(unsigned long long) * 2 * sms);
+  cudaMalloc(&sink, sizeof(float) * 256 * sms);
+  std::vector<unsigned long long> h(2 * sms);
+  int rc = 0;
+
+  if (all || !std::strcmp(which, "tma")) {
+    const int heads = 16, S = 4096, n_tiles = S / BN;
+    void *K = nullptr, *V = nullptr;
+    const size_t bytes = static_cast<size_t>(heads) * S * D * 2;
+    cudaMalloc(&K, bytes);
+    cudaMalloc(&V, bytes);
+    cudaMemset(K, 0, bytes);
+    cudaMemset(V, 0, bytes);
+    CUtensorMap mk, mv;
+    if (!make_map(&mk, K, heads, S) || !make_map(&mv, V, heads, S)) {
+      std::printf("tma: tensor map encoding failed\n");
+      return 1;
+    }
+    constexpr int ST = 5;
+    const int smem = ST * TILE_BYTES + 1024;
+    cudaFuncSetAttribute(tma_probe<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    for (int rep = 0; rep < 2; ++rep) tma_probe<ST><<<sms, 64, smem>>>(mk, mv, heads, n_tiles, cyc);
+    if (!check("tma")) return 1;
+    cudaMemcpy(h.data(), cyc, sizeof(unsigned long long) * sms, cudaMemcpyDeviceToHost);
+    const double c = mean_of(h, 1, 0, sms) / n_tiles;
+    const double gbs = 2.0 * TILE_BYTES / c * clk_khz * 1e3 / 1e9;
+    std::printf("tma      K+V tile pair (2 x %d KB, %d-slot ring, 16 heads x %d rows, %d CTAs): "
+                "%.0f cycles  (%.0f GB/s per SM, %.0f GB/s all SMs at %.0f MHz)\n",
+                TILE_BYTES / 1024, ST, S, sms, c, gbs, gbs * sms, clk_khz / 1e3);
+    cudaFree(K);
+    cudaFree(V);
+  }
+
+  if (all || !std::strcmp(which, "mma")) {
+    cudaFuncSetAttribute(mma_probe, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_SMEM);
+    const char* names[] = {"PV0 S0 PV1 S1, one issuer (kernel order)", "one issuer per Q tile (2 warps)",
+                           "PV0 PV1 S0 S1, one issuer", "S0 S1 only", "PV0 PV1 only"};
+    const double work[] = {2048, 2048, 2048, 1024, 1024};
+    const int iters = 256;
+    for (int o = 0; o < 5; ++o) {
+      cudaMemset(cyc, 0, sizeof(unsigned long long) * 2 * sms);
+      for (int rep = 0; rep < 2; ++rep) mma_probe<<<sms, 128, MMA_SMEM>>>(o, iters, cyc);
+      if (!check("mma")) return 1;
+      cudaMemcpy(h.data(), cyc, sizeof(unsigned long long) * 2 * sms, cudaMemcpyDeviceToHost);
+      double c = mean_of(h, 2, 0, sms);
+      if (o == kTwoIssuers) c = std::max(c, mean_of(h, 2, 1, sms));
+      c /= iters;
+      std::printf("mma      %-42s %6.0f cycles / iteration  (tensor work %4.0f: %.0f %%)\n", names[o], c,
+                  work[o], 100.0 * work[o] / c);
+    }
+  }
+
+  if (all || !std::strcmp(which, "softmax")) {
+    const int iters = 256;
+    cudaMemset(cyc, 0, sizeof(unsigned long long) * 2 * sms);
+    for (int rep = 0; rep < 2; ++rep) softmax_probe<1><<<sms, 128>>>(iters, cyc, sink);
+    if (!check("softmax")) return 1;
+    cudaMemcpy(h.data(), cyc, sizeof(unsigned long long) * 2 * sms, cudaMemcpyDeviceToHost);
+    std::printf("softmax  128 x %d tile, one warpgroup per SM:   %6.0f cycles / tile\n", BN,
+                mean_of(h, 2, 0, sms) / iters);
+    cudaMemset(cyc, 0, sizeof(unsigned long long) * 2 * sms);
+    for (int rep = 0; rep < 2; ++rep) softmax_probe<2><<<sms, 256>>>(iters, cyc, sink);
+    if (!check("softmax")) return 1;
+    cudaMemcpy(h.data(), cyc, sizeof(unsigned long long) * 2 * sms, cudaMemcpyDeviceToHost);
+    std::printf("softmax  128 x %d tile, two warpgroups per SM:  %6.0f / %6.0f cycles / tile "
+                "(MUFU floor %d per warpgroup alone)\n",
+                BN, mean_of(h, 2, 0, sms) / iters, mean_of(h, 2, 1, sms) / iters, BN * 8);
+  }
+  cudaFree(cyc);
+  cudaFree(sink);
+  return rc;
+}
