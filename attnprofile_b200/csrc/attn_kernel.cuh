@@ -168,7 +168,7 @@ struct AttnConfig {
   static constexpr int DBLK = D / 64;  // 64-element (128 B) column blocks per row
 
   // TMEM columns (32-bit each).  S_i (and P_i over it) then O_i.
-  static constexpr int NSBUF = (NQ == 1 && 2 * BN + D <= 512) ? 2 : 1;
+  static constexpr int NSBUF = (NQ * (2 * BN + D) <= 512) ? 2 : 1;
   static constexpr int TMEM_S_COLS = NQ * NSBUF * BN;
   static constexpr int TMEM_O_COL = TMEM_S_COLS;
   static constexpr int TMEM_USED = TMEM_S_COLS + NQ * D;
@@ -212,6 +212,17 @@ struct AttnConfig {
   static constexpr int LOAD_WARP = NUM_SOFTMAX_WARPS;
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;
   static constexpr int OBSERVER_WARP = NUM_SOFTMAX_WARPS + 2;  // profiler only
+  // MMA issuers.  With one S buffer per Q tile (NSBUF = 1) a single thread
+  // issues both tiles' MMAs in turn, which keeps the two softmax steps taking
+  // turns (each tile's next S waits for its own P V anyway).  With S double
+  // buffered (NQ = 2, BN <= 64 at D = 128) S_i(j+1) is ready before the
+  // softmax of S_i(j) ends, and an in-order issuer would make tile 0 wait for
+  // tile 1's P: one issuer per Q tile (MMA_WARP for tile 0, MMA_WARP2 for
+  // tile 1) lets both softmax warpgroups run back to back (C2 at 256 x 64:
+  // 742 -> 1030 TFLOP/s).  Each K/V slot is then released by NUM_ISSUERS
+  // commits.
+  static constexpr int NUM_ISSUERS = (NQ == 2 && NSBUF == 2) ? 2 : 1;
+  static constexpr int MMA_WARP2 = NUM_SOFTMAX_WARPS + 3;
   static constexpr int NUM_THREADS = 32 * (NUM_SOFTMAX_WARPS + 4);
   // One 128-row Q tile with narrow key tiles fits two CTAs per SM (shared
   // and tensor memory); the register budget is capped to keep that possible.
@@ -388,13 +399,14 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
 // ----------------------------------------------------------------------------
 template <class C, bool PROFILE>
 __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, const AttnParams& p,
-                         const WaitCtx& w, const Prof<PROFILE>& prof) {
+                         const WaitCtx& w, const Prof<PROFILE>& prof, int i0, int i1) {
+  // Issues the MMAs of Q tiles [i0, i1) of this CTA.
   auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
   const int n = wt.n;
   bool ok = true;
 
-  for (int i = 0; i < C::NQ && ok; ++i) ok = wait_bar(bar(C::BAR_Q + i), 0, w, kSiteQ);
-  if (ok) prof.stamp(kPhLoadQ, 0, 1);
+  for (int i = i0; i < i1 && ok; ++i) ok = wait_bar(bar(C::BAR_Q + i), 0, w, kSiteQ);
+  if (ok && i0 == 0) prof.stamp(kPhLoadQ, 0, 1);
 
   int t = 0;
   // Wait for ring item t (K_j when is_k, else V_j) to land in its slot.
@@ -403,7 +415,7 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
     const bool r = wait_bar(bar(C::BAR_KV_FULL + stage), (t / C::STAGES) & 1, w, kSiteKvFull);
     ++t;
     if (r) {
-      prof.stamp(is_k ? kPhLoadK : kPhLoadV, j, 1);
+      if (i0 == 0) prof.stamp(is_k ? kPhLoadK : kPhLoadV, j, 1);
       ptx::tc_fence_after();
     }
     return r;
@@ -452,7 +464,7 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
   for (int jj = 0; jj < C::NSBUF && jj < n && ok; ++jj) {
     int sk;
     if (!(ok = ring_wait(sk, true, jj))) break;
-    for (int i = 0; i < C::NQ; ++i) {
+    for (int i = i0; i < i1; ++i) {
       if (i == 0) prof.stamp(kPhQK, jj, 0);
       issue_s(i, jj, sk);
       ptx::mma_commit(bar(C::BAR_S_FULL + i * C::NSBUF + jj % C::NSBUF));
@@ -465,7 +477,7 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
     if (!(ok = ring_wait(sv, false, j))) break;
     const int jn = j + C::NSBUF;
     int sk = -1;
-    for (int i = 0; i < C::NQ && ok; ++i) {
+    for (int i = i0; i < i1 && ok; ++i) {
       const int pb = C::BAR_P_READY + (i * C::NSBUF + j % C::NSBUF) * C::PHALVES;
       constexpr int KSTEPS = C::BN / 16;
 #pragma unroll
@@ -908,7 +920,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
     for (int i = 0; i < C::NQ; ++i) ptx::mbar_init(bar(C::BAR_Q + i), 1);
     for (int s = 0; s < C::STAGES; ++s) {
       ptx::mbar_init(bar(C::BAR_KV_FULL + s), 1);
-      ptx::mbar_init(bar(C::BAR_KV_EMPTY + s), 1);
+      ptx::mbar_init(bar(C::BAR_KV_EMPTY + s), C::NUM_ISSUERS);
     }
     for (int i = 0; i < C::NQ * C::NSBUF; ++i) ptx::mbar_init(bar(C::BAR_S_FULL + i), 1);
     for (int i = 0; i < C::NQ * C::NSBUF * C::PHALVES; ++i)
@@ -917,7 +929,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
       ptx::mbar_init(bar(C::BAR_O_DONE + i), 1);
       ptx::mbar_init(bar(C::BAR_O_FINAL + i), 1);
     }
-    ptx::mbar_init(bar(C::BAR_DRAIN), 1);
+    ptx::mbar_init(bar(C::BAR_DRAIN), C::NUM_ISSUERS);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -948,7 +960,9 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
     if (warp == C::LOAD_WARP) {
       if (lane == 0) load_role<C, PROFILE>(&tmQ, &tmK, &tmV, sbase, wt, p, w, prof);
     } else if (warp == C::MMA_WARP) {
-      if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, wt, p, w, prof);
+      if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, wt, p, w, prof, 0, C::NUM_ISSUERS == 2 ? 1 : C::NQ);
+    } else if (C::NUM_ISSUERS == 2 && warp == C::MMA_WARP2) {
+      if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, wt, p, w, prof, 1, 2);
     } else if (warp == C::OBSERVER_WARP) {
       if constexpr (PROFILE) {
         if (lane == 0 && prof.buf != nullptr) observer_role<C>(sbase, wt.n, w, prof);

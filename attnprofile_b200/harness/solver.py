@@ -29,14 +29,14 @@ MMA_M_B200 = 128
 
 def tmem_columns(BM: int, BN: int, HD: int) -> int:
     nq = BM // MMA_M_B200
-    nsbuf = 2 if (nq == 1 and 2 * BN + HD <= TMEM_COLS) else 1
+    nsbuf = 2 if nq * (2 * BN + HD) <= TMEM_COLS else 1
     return nq * nsbuf * BN + nq * HD
 
 
 def smem_bytes(BM: int, BN: int, HD: int, stages: int) -> int:
     """Dynamic shared memory of the kernel variant (mirrors AttnConfig)."""
     nq = BM // MMA_M_B200
-    nsbuf = 2 if (nq == 1 and 2 * BN + HD <= TMEM_COLS) else 1
+    nsbuf = 2 if nq * (2 * BN + HD) <= TMEM_COLS else 1
     phalves = 2 if BN >= 64 else 1
     off_bar = nq * 128 * HD * 2 + stages * BN * HD * 2
     num_bars = nq + 2 * stages + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1
