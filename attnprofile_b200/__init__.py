@@ -26,7 +26,8 @@ ERR = {
 }
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
-SUPPORTED_TILES = [(128, 32), (128, 64), (128, 128), (128, 256), (256, 32), (256, 64), (256, 128)]
+SUPPORTED_TILES = [(128, 32), (128, 64), (128, 96), (128, 128), (128, 256), (256, 32), (256, 64),
+                   (256, 96), (256, 128)]
 
 _lib = None
 

@@ -25,10 +25,12 @@ inline VariantInfo variant_info() {
 #define ATTNPROF_FOR_EACH_TILE(X) \
   X(128, 32)                      \
   X(128, 64)                      \
+  X(128, 96)                      \
   X(128, 128)                     \
   X(128, 256)                     \
   X(256, 32)                      \
   X(256, 64)                      \
+  X(256, 96)                      \
   X(256, 128)
 
 template <typename T, int D, bool PROFILE>

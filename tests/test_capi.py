@@ -56,8 +56,8 @@ def test_shard_range_rejects_bad_rank(engine):
     assert engine.lib().attn_shard_range(16, 4, 4, ctypes.byref(b), ctypes.byref(e)) == -8
 
 
-@pytest.mark.parametrize("bm,bn", [(128, 32), (128, 64), (128, 128), (128, 256), (256, 32),
-                                   (256, 64), (256, 128)])
+@pytest.mark.parametrize("bm,bn", [(128, 32), (128, 64), (128, 96), (128, 128), (128, 256),
+                                   (256, 32), (256, 64), (256, 96), (256, 128)])
 @pytest.mark.parametrize("d", [64, 128])
 def test_query_config_fits_b200(engine, bm, bn, d):
     for dt in (0, 1):

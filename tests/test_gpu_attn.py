@@ -23,7 +23,8 @@ pytestmark = pytest.mark.gpu
 
 MAX_ABS = 2e-3
 MEAN_ABS = 2e-4
-TILES = [(128, 32), (128, 64), (128, 128), (128, 256), (256, 32), (256, 64), (256, 128)]
+TILES = [(128, 32), (128, 64), (128, 96), (128, 128), (128, 256), (256, 32), (256, 64), (256, 96),
+         (256, 128)]
 GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
 
 
