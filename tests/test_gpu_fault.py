@@ -21,16 +21,26 @@ def test_bounded_wait_reports_timeout_and_context_survives(engine):
     engine.set_timeout_ns(50_000_000)  # 50 ms
     try:
         engine.debug_fault(1)
-        for bm in (128, 256):
-            engine.attn(Q, K, V, BM=bm, BN=128)
+        # one MMA issuer (NSBUF = 1), one issuer per Q tile (256 x 64, 256 x 32),
+        # and a key-split launch whose parts never count in
+        for bm, bn, split in ((128, 128, 0), (256, 128, 0), (256, 64, 0), (256, 32, 0),
+                              (256, 128, 2)):
+            engine.set_split(split)
+            engine.attn(Q, K, V, BM=bm, BN=bn)
             rc, site = engine.get_status(0, reset=True)
-            assert rc == engine.ERR["DEVICE_TIMEOUT"], (rc, hex(site))
+            assert rc == engine.ERR["DEVICE_TIMEOUT"], (bm, bn, split, rc, hex(site))
             assert site & 0xFF00 == 0x7100
     finally:
         engine.debug_fault(0)
+        engine.set_split(0)
         engine.set_timeout_ns(2_000_000_000)
-    O = engine.attn(Q, K, V, BM=256, BN=128)
-    torch.cuda.synchronize()
-    assert engine.get_status(0)[0] == 0
     ref = torch.softmax((Q.float() @ K.float().transpose(-1, -2)) / 128 ** 0.5, -1) @ V.float()
-    assert (O.float() - ref).abs().max().item() < 2e-3
+    for bm, bn, split in ((256, 128, 0), (256, 64, 0), (256, 128, 2)):
+        engine.set_split(split)
+        try:
+            O = engine.attn(Q, K, V, BM=bm, BN=bn)
+            torch.cuda.synchronize()
+        finally:
+            engine.set_split(0)
+        assert engine.get_status(0)[0] == 0
+        assert (O.float() - ref).abs().max().item() < 2e-3, (bm, bn, split)
