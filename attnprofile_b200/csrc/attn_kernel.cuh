@@ -150,6 +150,15 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
 // (they stay in L2 for the merging CTA); the merge loads them with
 // ld.global.cg (L2, past L1), since other CTAs wrote them.
 
+// Of every 8 (column-pair) exponentials in a softmax chunk, kPolyPairsOf8
+// run as the FMA-pipe polynomial (ptx::exp2_poly_pair) and the rest on the
+// MUFU unit, so the two pipes share the B*H*S^2 exponentials.  -1 (default):
+// per variant (AttnConfig::POLY8); 0..8 forces that share for every variant.
+#ifndef ATTNPROF_POLY_PAIRS_OF_8
+#define ATTNPROF_POLY_PAIRS_OF_8 -1
+#endif
+constexpr int kPolyPairsOf8 = ATTNPROF_POLY_PAIRS_OF_8;
+
 template <typename T, int D_, int BN_, int NQ_, int STAGES_>
 struct AttnConfig {
   static constexpr int D = D_;
@@ -195,7 +204,12 @@ struct AttnConfig {
   // P is published in PHALVES parts so P V can start on the first keys while
   // the softmax computes the rest: with >= 2 chunks of 32 columns, part 0 is
   // the first PSPLIT_CHUNKS chunks (P V K-steps [0, 2 * PSPLIT_CHUNKS)).
-  static constexpr int PHALVES = BN >= 64 ? 2 : 1;
+  // Variants that double-buffer S at D = 64 keep both softmax warpgroups on
+  // the exponentials back to back, where the MUFU unit is the bound: there a
+  // quarter of the exponentials go to the FMA pipe and P is published in one
+  // piece (C3 at 256 x 96: 631 -> 664 TFLOP/s).  At D = 128 neither helps.
+  static constexpr bool EXP_BOUND = NQ == 2 && D == 64 && NQ * (2 * BN + D) <= 512;
+  static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND) ? 2 : 1;
   static constexpr int PSPLIT_CHUNKS = BN / 64;
   static constexpr int BAR_P_READY = BAR_S_FULL + NQ * NSBUF;      // [NQ][NSBUF][PHALVES]
   static constexpr int BAR_O_DONE = BAR_P_READY + NQ * NSBUF * PHALVES;  // every P V of tile i
@@ -235,6 +249,7 @@ struct AttnConfig {
   static_assert(NQ != 2 || 2 * 128 * REG_SOFTMAX + 128 * REG_OTHER <= 384 * 168,
                 "register split exceeds the launch allocation");
 
+  static constexpr int POLY8 = kPolyPairsOf8 >= 0 ? kPolyPairsOf8 : (EXP_BOUND ? 2 : 0);
   static constexpr uint32_t IDESC_S = ptx::idesc_f16(128, BN, kBF16, false);
   static constexpr uint32_t IDESC_PV = ptx::idesc_f16(128, D, kBF16, true);
 };
@@ -245,18 +260,12 @@ struct AttnConfig {
 // accumulators all hold exactly enough.
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
-// Of every 8 (column-pair) exponentials in a softmax chunk, this many run as
-// the FMA-pipe polynomial (ptx::exp2_poly_pair) and the rest on the MUFU
-// unit, so the two pipes share the B*H*S^2 exponentials.
-#ifndef ATTNPROF_POLY_PAIRS_OF_8
-#define ATTNPROF_POLY_PAIRS_OF_8 0
-#endif
-constexpr int kPolyPairsOf8 = ATTNPROF_POLY_PAIRS_OF_8;
 
 // Which column pairs of a 32-column chunk take the polynomial: spread evenly
 // (e.g. 4 of 8 -> every other pair) so both pipes stay busy.
+template <int POLY8>
 __host__ __device__ constexpr bool poly_pair(int e) {
-  return kPolyPairsOf8 > 0 && ((e % 8) * kPolyPairsOf8) % 8 + kPolyPairsOf8 > 7;
+  return POLY8 > 0 && ((e % 8) * POLY8) % 8 + POLY8 > 7;
 }
 
 // Row maximum of N register values with independent partial maxima (short
@@ -644,7 +653,7 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       for (int e = 0; e < 16; ++e) {
         const int c0 = (KEEP ? c * 32 : 0) + 2 * e;
         float p0, p1;
-        if (poly_pair(e)) {
+        if (poly_pair<C::POLY8>(e)) {
           ptx::exp2_poly_pair(__uint_as_float(sreg[c0]), __uint_as_float(sreg[c0 + 1]), poly_a,
                               poly_b, p0, p1);
         } else {

@@ -37,7 +37,8 @@ def smem_bytes(BM: int, BN: int, HD: int, stages: int) -> int:
     """Dynamic shared memory of the kernel variant (mirrors AttnConfig)."""
     nq = BM // MMA_M_B200
     nsbuf = 2 if nq * (2 * BN + HD) <= TMEM_COLS else 1
-    phalves = 2 if BN >= 64 else 1
+    exp_bound = nq == 2 and HD == 64 and nq * (2 * BN + HD) <= TMEM_COLS
+    phalves = 2 if (BN >= 64 and not exp_bound) else 1
     off_bar = nq * 128 * HD * 2 + stages * BN * HD * 2
     num_bars = nq + 2 * stages + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1
     off_misc = off_bar + ((num_bars * 8 + 15) // 16) * 16
