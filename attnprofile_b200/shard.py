@@ -62,3 +62,35 @@ def sum_over_ranks(value: int, device=None) -> int:
     t = torch.tensor([int(value)], dtype=torch.int64, device=device)
     dist.all_reduce(t)
     return int(t.item())
+
+
+def gather_output(O_local, units_total: int, dst: int = 0):
+    """Collect the sharded output on one rank: every rank holds O for its
+    units [u0, u1) as [1, u1 - u0, S, D]; rank `dst` returns the whole
+    [1, units_total, S, D] (other ranks return None).  Point-to-point sends of
+    each shard straight into its slice of the destination tensor (NCCL over
+    NVLink on GPUs, gloo on CPU) -- the optional consumer-side step after the
+    collective-free compute.  Identity with one rank."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return O_local
+    world, rank = dist.get_world_size(), dist.get_rank()
+    u0, u1 = shard_range(units_total, world, rank)
+    if O_local.shape[1] != u1 - u0:
+        raise ValueError(f"rank {rank} holds {O_local.shape[1]} units, its range is [{u0}, {u1})")
+    if rank != dst:
+        if u1 > u0:
+            dist.send(O_local.contiguous(), dst)
+        return None
+    S, D = O_local.shape[2], O_local.shape[3]
+    out = torch.empty(1, units_total, S, D, dtype=O_local.dtype, device=O_local.device)
+    out[:, u0:u1].copy_(O_local)
+    ops = []
+    for r in range(world):
+        r0, r1 = shard_range(units_total, world, r)
+        if r != dst and r1 > r0:
+            ops.append(dist.P2POp(dist.irecv, out[:, r0:r1], r))
+    for req in (dist.batch_isend_irecv(ops) if ops else []):
+        req.wait()
+    return out

@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gather", action="store_true",
+                    help="N > 1: after timing, collect the sharded O on rank 0 over NCCL "
+                         "point-to-point and report its time separately")
     ap.add_argument("--preroll-s", type=float, default=0.5,
                     help="untimed back-to-back launches before timing (clock warm-up)")
     a = ap.parse_args()
@@ -397,6 +400,24 @@ def main():
 
     launches = shard.sum_over_ranks(args.steps, dev)
 
+    # Optional consumer-side step, outside the metric: the last step's O
+    # shards gathered on rank 0 (NVLink point-to-point through NCCL).
+    gather = None
+    if args.gather and n > 1:
+        O_last = sets[(args.steps - 1) % n_sets][3]
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for rep in range(2):  # the first call sets up NCCL's point-to-point channels
+            barrier()
+            torch.cuda.synchronize()
+            g0.record(stream)
+            shard.gather_output(O_last, units_total, dst=0)
+            g1.record(stream)
+            torch.cuda.synchronize()
+        g_ms = shard.max_over_ranks(g0.elapsed_time(g1), dev)
+        g_bytes = units_total * S * D * elt * (n - 1) // n
+        gather = {"ms": g_ms, "bytes_to_rank0": g_bytes, "GB_per_s": g_bytes / (g_ms * 1e-3) / 1e9,
+                  "how": "torch.distributed send / batch_isend_irecv (NCCL) into rank 0's [1, B*H, S, D]"}
+
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_reference(args.workload)
@@ -419,6 +440,8 @@ def main():
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
         }
+        if gather is not None:
+            line["gather"] = gather
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -106,3 +106,34 @@ def test_rank_failure_is_seen_by_the_others(tmp_path):
         p.join(timeout=60)
     assert all(not p.is_alive() for p in ctx.processes)
     assert (tmp_path / "rank0.txt").read_text().startswith("error")
+
+
+def _gather_worker(rank, world, port, out_dir):
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+    from attnprofile_b200 import shard
+    _init(rank, world, port)
+    units = 7  # uneven shards (and an empty one at world 8 would be allowed)
+    u0, u1 = shard.shard_range(units, world, rank)
+    # stand-in output: each unit's block filled with its unit index
+    O = torch.arange(u0, u1, dtype=torch.float32).view(1, -1, 1, 1).expand(1, u1 - u0, 5, 4)
+    O = O.contiguous().to(torch.float16)
+    full = shard.gather_output(O, units, dst=world - 1)
+    if rank == world - 1:
+        torch.save(full, Path(out_dir) / "full.pt")
+    else:
+        assert full is None
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_output_collects_every_shard(tmp_path, world):
+    import torch
+    import torch.multiprocessing as mp
+    mp.start_processes(_gather_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    full = torch.load(tmp_path / "full.pt")
+    assert tuple(full.shape) == (1, 7, 5, 4)
+    for u in range(7):
+        assert torch.all(full[0, u] == u)
