@@ -8,7 +8,8 @@
 //   * one TMA producer warp loads the Q tile(s) once and streams K and V tiles
 //     through a STAGES-deep ring of 128B-swizzled shared-memory slots guarded
 //     by full/empty mbarrier pairs;
-//   * one MMA warp (a single elected lane) issues tcgen05.mma:
+//   * one MMA warp (a single elected lane; one per Q tile when S is
+//     double-buffered in a two-tile CTA) issues tcgen05.mma:
 //       S_i = Q_i K_j^T    (A, B from shared memory, D in TMEM, f32)
 //       O_i += P_i V_j     (A = P read from TMEM, B = V from shared memory)
 //     and signals completion with tcgen05.commit onto mbarriers;
@@ -20,11 +21,14 @@
 //   * the same warpgroups finish the tile: O / rowsum, convert, stage in the
 //     (now free) Q shared-memory slot with the TMA 128B swizzle, TMA store.
 //
-// BM = 128 * NQ rows of Q per CTA.  With NQ = 2 the two softmax warpgroups
-// ping-pong: while one runs exp2 on its S tile the tensor core runs the other
-// tile's P V and next Q K^T.  With NQ = 1 the S accumulator is double-buffered
-// in TMEM when it fits (2 * BN + D <= 512 columns) so Q K_{j+1}^T overlaps the
-// softmax of tile j.
+// BM = 128 * NQ rows of Q per CTA (a unit), or one key range of a unit when
+// the launch splits its last wave along the keys (WorkTile; the parts' partial
+// results are merged by the part that finishes last).  With NQ = 2 and one S
+// buffer per Q tile the two softmax warpgroups ping-pong: while one runs exp2
+// on its S tile the tensor core runs the other tile's P V and next Q K^T.  The
+// S accumulator is double-buffered in TMEM whenever it fits
+// (NQ * (2 * BN + D) <= 512 columns) so Q K_{j+1}^T overlaps the softmax of
+// tile j; two-tile CTAs then issue each tile's MMAs from its own warp.
 //
 // Every wait is bounded (see wait_bar): on expiry the kernel records an error
 // code in a device status word, raises a CTA-local abort flag so the other
@@ -958,8 +962,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
   const uint32_t tmem = *tmem_slot;
 
   const WaitCtx w{abort_flag, p.status, p.timeout_ns};
-  const int cta_lin = blockIdx.y * gridDim.x + blockIdx.x;
-  Prof<PROFILE> prof{(PROFILE && cta_lin == p.prof_cta) ? p.prof : nullptr};
+  Prof<PROFILE> prof{(PROFILE && static_cast<int>(blockIdx.x) == p.prof_cta) ? p.prof : nullptr};
 
   if (warp < C::NUM_SOFTMAX_WARPS) {
     if constexpr (C::NQ == 2) ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
