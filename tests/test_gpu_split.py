@@ -126,3 +126,29 @@ def test_plan_for_benchmark_shapes(engine):
         assert p["workspace_bytes"] >= 108 * 4 * 256 * (128 * 4 + 8)
     engine.set_split(1)
     assert engine.query_split(1, 1, 16384, 128)["split"] == 1
+
+
+def test_split_padded_layout_writes_only_valid_rows(engine, oracle_mod):
+    """attn_fwd_padded with a forced split: the merging part's TMA store goes
+    through the padded map, rows >= S stay untouched."""
+    torch = _torch()
+    B, H, S, D, BM, BN = 1, 2, 300, 128, 256, 128
+    SQO, SKV = 512, 384
+    q, k, v = make_inputs(B, H, S, D, torch.float16, seed=15)
+    Qp = torch.full((B, H, SQO, D), float("nan"), dtype=torch.float16)
+    Kp = torch.full((B, H, SKV, D), float("nan"), dtype=torch.float16)
+    Vp = torch.full((B, H, SKV, D), float("nan"), dtype=torch.float16)
+    Qp[:, :, :S], Kp[:, :, :S], Vp[:, :, :S] = q, k, v
+    Op = torch.full((B, H, SQO, D), 7.0, dtype=torch.float16).cuda()
+    engine.set_split(3)
+    try:
+        engine.attn_padded(Qp.cuda(), Kp.cuda(), Vp.cuda(), Op, S, BM=BM, BN=BN)
+        torch.cuda.synchronize()
+    finally:
+        engine.set_split(0)
+    assert engine.get_status(0)[0] == 0
+    O = Op.cpu()
+    assert torch.all(O[:, :, S:] == 7.0), "padding rows of O were written"
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
+    mx, mean = compare(oracle_mod, to_u16(O[:, :, :S]), ref, 0)
+    assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
