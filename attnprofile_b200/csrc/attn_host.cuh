@@ -250,7 +250,7 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   static_assert(C::SMEM_BYTES <= kSmemLimit, "shared memory over the sm_100 per-CTA limit");
   const int dtype = std::is_same<T, __half>::value ? ATTN_DTYPE_F16 : ATTN_DTYPE_BF16;
   const long long BH = static_cast<long long>(B) * H;
-  if (BH > 65535) return ATTN_ERR_INVALID_ARG;
+  if (BH > INT_MAX) return ATTN_ERR_INVALID_ARG;  // the grid is 1-D over work tiles
 
   auto kern = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE>;
   static bool attr_done[64] = {};

@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <climits>
 #include <mutex>
 #include <vector>
 
@@ -52,7 +53,7 @@ static int validate(const void* Q, const void* K, const void* V, const void* O, 
   if (B == 0 || H == 0 || S == 0) return ATTN_OK;  // empty problem: nothing to do
   if (!Q || !K || !V || !O) return ATTN_ERR_INVALID_ARG;
   if (SQO < S || SKV < S) return ATTN_ERR_INVALID_ARG;
-  if (static_cast<long long>(B) * H > 65535) return ATTN_ERR_INVALID_ARG;
+  if (static_cast<long long>(B) * H > INT_MAX) return ATTN_ERR_INVALID_ARG;
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return ATTN_ERR_MISALIGNED;
   return 1;  // proceed
 }

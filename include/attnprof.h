@@ -45,7 +45,7 @@ extern "C" {
  * attn_fwd -- one attention forward over contiguous [B, H, S, D] tensors.
  * BM in {128, 256} query rows per CTA; BN in {32, 64, 96, 128, 256} keys per
  * KV tile (BM = 256 with BN = 256 does not fit tensor memory: UNSUPPORTED).
- * D in {64, 128}.  B*H <= 65535.  Asynchronous; returns launch errors only
+ * D in {64, 128}.  Asynchronous; returns launch errors only
  * (device-side timeouts are reported by attn_get_status).
  * Replaces: runAttn<...>(Q, K, V, O)            tuning/attn_test.cu:1665-1691
  *           (BM, BN as run-time values instead of template parameters).

@@ -88,7 +88,8 @@ def test_host_validation_without_gpu(engine):
     assert L.attn_fwd(good + 2, good, good, good, 1, 1, 16, 128, 0, 128, 128, None) == -3
     assert L.attn_fwd(good, good, good, good, 1, 1, 16, 96, 0, 128, 128, None) == -2
     assert L.attn_fwd(good, good, good, good, 1, 1, 16, 128, 7, 128, 128, None) == -2
-    assert L.attn_fwd(good, good, good, good, 1, 65536, 16, 128, 0, 128, 128, None) == -1
+    # B*H beyond a 32-bit count (the grid is 1-D over work tiles, no 65535 limit)
+    assert L.attn_fwd(good, good, good, good, 65536, 65536, 16, 128, 0, 128, 128, None) == -1
     # padded rows fewer than S
     assert L.attn_fwd_padded(good, good, good, good, 1, 1, 64, 128, 32, 64, 0, 128, 128,
                              None) == -1

@@ -186,3 +186,20 @@ def test_parity_moving_row_max(engine, oracle_mod, BM, BN, ramp):
     ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
     mx, mean = compare(oracle_mod, to_u16(out), ref, 0)
     assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
+
+
+def test_more_than_65535_heads(engine, oracle_mod):
+    """B*H above the 65535 of a 2-D grid's y dimension: the 1-D grid of work
+    tiles runs them (the reference's grid {SQO/BM, H, B} caps H at 65535)."""
+    torch = _torch()
+    B, H, S, D = 2, 35000, 16, 64
+    g = torch.Generator(device="cuda").manual_seed(3)
+    Q, K, V = (torch.randn(B, H, S, D, generator=g, device="cuda").half() for _ in range(3))
+    O = engine.attn(Q, K, V, BM=128, BN=64)
+    torch.cuda.synchronize()
+    assert engine.get_status(0)[0] == 0
+    for b, h in ((0, 0), (1, H - 1), (0, 12345)):
+        u16 = lambda t: to_u16(t[b:b + 1, h:h + 1].cpu())
+        ref = oracle_mod.attention(u16(Q), u16(K), u16(V), bn_tile=64)
+        mx, mean = compare(oracle_mod, u16(O), ref, 0)
+        assert mx <= 1.0 and mean <= MEAN_ABS, (b, h, mx, mean)
