@@ -891,13 +891,15 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
 }
 
 // Profiler observer: stamps the completion of each P V of Q tile 0.  It only
-// watches; a missed phase costs a stamp, never an error status.
+// watches; a missed phase costs a stamp, never an error status.  It waits
+// with a suspend hint so it does not take issue slots from the softmax warps
+// of its SM sub-partition (a polling observer slowed them visibly).
 template <class C>
 __device__ void observer_role(uint32_t sbase, int n, const WaitCtx& w, const Prof<true>& prof) {
   const uint32_t bar = sbase + C::OFF_BAR + 8u * (C::BAR_O_DONE + 0);
   for (int j = 0; j < n; ++j) {
     const unsigned long long t0 = ptx::globaltimer_ns();
-    while (!ptx::mbar_try_wait(bar, j & 1)) {
+    while (!ptx::mbar_try_wait_sleep(bar, j & 1, 100000u)) {
       if (*w.abort || ptx::globaltimer_ns() - t0 > w.timeout_ns) return;
     }
     prof.stamp(kPhPV, j, 1);

@@ -49,6 +49,22 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 // One probe of the phase with the given parity; true once that phase has
 // completed.  try_wait may suspend the thread for a short, hardware-defined
 // window before returning false, so a loop over it does not burn issue slots.
+// try_wait with a suspend-time hint: the thread may sleep up to `ns`
+// nanoseconds inside the instruction (it resumes when the phase completes),
+// so a waiting warp does not take issue slots from the warps sharing its SM
+// sub-partition by re-polling.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
