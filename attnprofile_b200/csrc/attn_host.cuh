@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cmath>
 #include <cstdint>
@@ -253,26 +254,33 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   if (BH > INT_MAX) return ATTN_ERR_INVALID_ARG;  // the grid is 1-D over work tiles
 
   auto kern = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE>;
-  static bool attr_done[64] = {};
-  static int slots_of[64] = {};
+  // Per-device set-up of this variant (shared-memory attribute, resident CTAs
+  // per wave), once per device; thread-safe.
+  static std::mutex init_mu;
+  static std::atomic<int> slots_of[64];  // 0 until the device is set up
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return ATTN_ERR_CUDA;
-  if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
-        cudaSuccess)
-      return ATTN_ERR_RESOURCE;
-    int sms = 0, occ = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, C::NUM_THREADS, C::SMEM_BYTES) !=
-            cudaSuccess)
-      return ATTN_ERR_CUDA;
-    if (occ < 1) return ATTN_ERR_RESOURCE;
-    slots_of[dev] = sms * occ;
-    attr_done[dev] = true;
+  int slots = dev < 64 ? slots_of[dev].load(std::memory_order_acquire) : 0;
+  if (slots == 0) {
+    std::lock_guard<std::mutex> g(init_mu);
+    slots = dev < 64 ? slots_of[dev].load(std::memory_order_relaxed) : 0;
+    if (slots == 0) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
+          cudaSuccess)
+        return ATTN_ERR_RESOURCE;
+      int sms = 0, occ = 0;
+      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, C::NUM_THREADS,
+                                                        C::SMEM_BYTES) != cudaSuccess)
+        return ATTN_ERR_CUDA;
+      if (occ < 1) return ATTN_ERR_RESOURCE;
+      slots = sms * occ;
+      if (dev < 64) slots_of[dev].store(slots, std::memory_order_release);
+    }
   }
   const long long qt = (S + C::BM - 1) / C::BM;
   const int n_kv = (S + BN - 1) / BN;
-  SplitPlan plan = plan_split(BH * qt, n_kv, dev < 64 ? slots_of[dev] : 148, o.split);
+  SplitPlan plan = plan_split(BH * qt, n_kv, slots, o.split);
   plan_workspace(&plan, C::BM, D, NQ, sizeof(float));
   if (o.plan_out) *o.plan_out = plan;
   if (o.plan_only) return ATTN_OK;

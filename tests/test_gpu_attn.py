@@ -203,3 +203,40 @@ def test_more_than_65535_heads(engine, oracle_mod):
         ref = oracle_mod.attention(u16(Q), u16(K), u16(V), bn_tile=64)
         mx, mean = compare(oracle_mod, u16(O), ref, 0)
         assert mx <= 1.0 and mean <= MEAN_ABS, (b, h, mx, mean)
+
+
+def test_concurrent_host_threads_on_separate_streams(engine):
+    """Four host threads launch on their own streams at once (first-use set-up
+    of several variants, tensor-map cache, status word): results equal the
+    single-threaded ones bit for bit."""
+    import threading
+    torch = _torch()
+    tiles = [(256, 128), (128, 64), (256, 64), (128, 128)]
+    inputs = [make_inputs(1, 4, 1000 + 64 * i, 128, torch.float16, seed=40 + i) for i in range(4)]
+    dev_inputs = [[x.cuda() for x in t] for t in inputs]
+    outs = [None] * 4
+    errors = []
+
+    def work(i):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                Q, K, V = dev_inputs[i]
+                O = engine.attn(Q, K, V, BM=tiles[i][0], BN=tiles[i][1], stream=s)
+                s.synchronize()
+                outs[i] = O.cpu()
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    assert engine.get_status(0)[0] == 0
+    for i in range(4):
+        Q, K, V = dev_inputs[i]
+        ref = engine.attn(Q, K, V, BM=tiles[i][0], BN=tiles[i][1])
+        torch.cuda.synchronize()
+        assert torch.equal(outs[i], ref.cpu()), i
