@@ -131,6 +131,8 @@ enum MmaOrder : int {
   kGrouped = 2,      // PV0, PV1, S0, S1 by one issuer
   kQkOnly = 3,       // S0, S1
   kPvOnly = 4,       // PV0, PV1
+  kQkN64 = 5,        // S0, S1 as 128 x 64 tiles (BN = 64): 8 MMAs of N = 64 each
+  kPvK64 = 6,        // PV0, PV1 over 64 keys (BN = 64): 4 MMAs each
 };
 
 __global__ void __launch_bounds__(128, 1) mma_probe(int order, int iters, unsigned long long* cycles) {
@@ -158,6 +160,7 @@ __global__ void __launch_bounds__(128, 1) mma_probe(int order, int iters, unsign
   const uint32_t q0 = base, k = base + 2 * 32768, v = base + 3 * 32768;
   const uint32_t id_s = ptx::idesc_f16(128, 128, false, false);
   const uint32_t id_pv = ptx::idesc_f16(128, 128, false, true);
+  const uint32_t id_s64 = ptx::idesc_f16(128, 64, false, false);
   auto qk = [&](int i) {
     const uint64_t qd = ptx::smem_desc_sw128(q0 + i * 32768, 16, 1024);
     const uint64_t kd = ptx::smem_desc_sw128(k, 16, 1024);
@@ -165,6 +168,21 @@ __global__ void __launch_bounds__(128, 1) mma_probe(int order, int iters, unsign
       const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
       ptx::mma_ss(tmem + i * 128, qd + off, kd + off, id_s, kk > 0 ? 1u : 0u);
     }
+  };
+  auto qk64 = [&](int i) {
+    const uint64_t qd = ptx::smem_desc_sw128(q0 + i * 32768, 16, 1024);
+    const uint64_t kd = ptx::smem_desc_sw128(k, 16, 1024);
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint64_t qo = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+      const uint64_t ko = static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+      ptx::mma_ss(tmem + i * 128, qd + qo, kd + ko, id_s64, kk > 0 ? 1u : 0u);
+    }
+  };
+  auto pv64 = [&](int i) {
+    const uint64_t vd = ptx::smem_desc_sw128(v, 64 * 128, 1024);
+    for (int kk = 0; kk < 4; ++kk)
+      ptx::mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
+                  vd + static_cast<uint64_t>(kk * 2048 >> 4), id_pv, 1u);
   };
   auto pv = [&](int i) {
     const uint64_t vd = ptx::smem_desc_sw128(v, 128 * 128, 1024);
@@ -186,6 +204,10 @@ __global__ void __launch_bounds__(128, 1) mma_probe(int order, int iters, unsign
         pv(0); pv(1); qk(0); qk(1);
       } else if (order == kQkOnly) {
         qk(0); qk(1);
+      } else if (order == kQkN64) {
+        qk64(0); qk64(1);
+      } else if (order == kPvK64) {
+        pv64(0); pv64(1);
       } else {
         pv(0); pv(1);
       }
@@ -360,10 +382,11 @@ int main(int argc, char** argv) {
   if (all || !std::strcmp(which, "mma")) {
     cudaFuncSetAttribute(mma_probe, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_SMEM);
     const char* names[] = {"PV0 S0 PV1 S1, one issuer (kernel order)", "one issuer per Q tile (2 warps)",
-                           "PV0 PV1 S0 S1, one issuer", "S0 S1 only", "PV0 PV1 only"};
-    const double work[] = {2048, 2048, 2048, 1024, 1024};
+                           "PV0 PV1 S0 S1, one issuer", "S0 S1 only", "PV0 PV1 only",
+                           "S0 S1 at BN=64 (N=64 MMAs)", "PV0 PV1 at BN=64 (K=64)"};
+    const double work[] = {2048, 2048, 2048, 1024, 1024, 512, 512};
     const int iters = 256;
-    for (int o = 0; o < 5; ++o) {
+    for (int o = 0; o < 7; ++o) {
       cudaMemset(cyc, 0, sizeof(unsigned long long) * 2 * sms);
       for (int rep = 0; rep < 2; ++rep) mma_probe<<<sms, 128, MMA_SMEM>>>(o, iters, cyc);
       if (!check("mma")) return 1;
