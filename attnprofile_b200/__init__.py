@@ -16,7 +16,8 @@ from ._build import LIB_PATH, build  # noqa: F401
 
 __all__ = [
     "AttnError", "attn", "attn_padded", "attn_profiled", "query_config", "get_status",
-    "set_timeout_ns", "debug_fault", "lib", "build", "ERR", "SUPPORTED_TILES", "attn_sharded",
+    "set_timeout_ns", "debug_fault", "lib", "build", "ERR", "SUPPORTED_TILES", "PAIR_TILES",
+    "attn_sharded",
     "shard_range",
 ]
 
@@ -28,6 +29,9 @@ DTYPE_F16 = 0
 DTYPE_BF16 = 1
 SUPPORTED_TILES = [(128, 32), (128, 64), (128, 96), (128, 128), (128, 256), (256, 32), (256, 64),
                    (256, 96), (256, 128)]
+# D = 128 only: a cluster of two 256-row CTAs sharing every K/V tile through
+# cta_group::2 (2-SM) tensor-core MMAs.
+PAIR_TILES = [(512, 128)]
 
 _lib = None
 
@@ -148,10 +152,11 @@ def profile_layout() -> tuple[int, int]:
 
 def attn_profiled(Q, K, V, O=None, *, BM: int = 256, BN: int = 128, cta: int = 0, stream=None):
     """One launch of the profiler-enabled variant; returns (O, stamps) where
-    stamps is an int64 CPU tensor [11 phases, 32 slots, 2] of clock64 values
-    (0 = not recorded).  Phases: LoadQ, LoadK, LoadV, GEMM-QK, SOFTMAX, GEMM-PV,
-    then the SOFTMAX steps S-ld, max, exp, P-st (slots = KV iterations), then
-    Epilogue (slots = steps, profiler.EPILOGUE_STEPS)."""
+    stamps is an int64 CPU tensor [phases, 32 slots, 2] of clock64 values
+    (0 = not recorded; geometry from profile_layout()).  Phases: LoadQ, LoadK,
+    LoadV, GEMM-QK, SOFTMAX, GEMM-PV, then the SOFTMAX steps S-ld, max, exp,
+    P-st (slots = KV iterations), then Epilogue (slots = steps,
+    profiler.EPILOGUE_STEPS), then the trace phases (profiler.TRACE_PHASES)."""
     import torch
     if O is None:
         O = torch.empty_like(Q)

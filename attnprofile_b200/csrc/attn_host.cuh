@@ -41,13 +41,15 @@ constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per CTA on s
 // CTA, or of each of two CTAs on an SM for the variants built for two
 // (AttnConfig::MIN_CTAS_PER_SM; the SM has 233472 bytes, 1 KB of which each
 // CTA reserves).
-template <typename T, int D, int BN, int NQ>
-constexpr int auto_stages(int cap = 8) {
-  using C2 = AttnConfig<T, D, BN, NQ, 2>;
+template <typename T, int D, int BN, int NQ, bool PAIR = false>
+constexpr int auto_stages(int cap = PAIR ? 12 : 8) {
+  using C2 = AttnConfig<T, D, BN, NQ, 2, PAIR>;
   const int limit = C2::MIN_CTAS_PER_SM == 2 ? 233472 / 2 - 1024 : kSmemLimit;
   int best = 0;
   for (int s = 2; s <= cap; ++s) {
-    if (C2::OFF_KV + s * (BN * D * 2) + 256 + 1024 + 16 <= limit) best = s;
+    const int bars = ((C2::NUM_BARS + 2 * (s - 2)) * 8 + 15) / 16 * 16;
+    if (C2::OFF_KV + s * C2::KV_TILE_BYTES + (bars > 256 ? bars : 256) + 1024 + 16 <= limit)
+      best = s;
   }
   return best;
 }
@@ -244,16 +246,32 @@ inline int get_tensor_map(CUtensorMap* out, const void* ptr, int dtype, int D, i
 // Per-device status word written by the kernel's bounded waits.
 int* device_status_ptr();
 
-template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE>
+template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE, bool PAIR = false>
 int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int H, int S,
                 long long q_rows, long long kv_rows, cudaStream_t stream, const LaunchOpts& o) {
-  using C = AttnConfig<T, D, BN, NQ, STAGES>;
+  using C = AttnConfig<T, D, BN, NQ, STAGES, PAIR>;
   static_assert(C::SMEM_BYTES <= kSmemLimit, "shared memory over the sm_100 per-CTA limit");
   const int dtype = std::is_same<T, __half>::value ? ATTN_DTYPE_F16 : ATTN_DTYPE_BF16;
   const long long BH = static_cast<long long>(B) * H;
   if (BH > INT_MAX) return ATTN_ERR_INVALID_ARG;  // the grid is 1-D over work tiles
 
-  auto kern = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE>;
+  auto kern = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE, PAIR>;
+  // CTA pairs run as clusters of two consecutive CTAs.
+  cudaLaunchAttribute cluster_attr{};
+  cluster_attr.id = cudaLaunchAttributeClusterDimension;
+  cluster_attr.val.clusterDim.x = C::CTAS;
+  cluster_attr.val.clusterDim.y = 1;
+  cluster_attr.val.clusterDim.z = 1;
+  auto launch_cfg = [&](unsigned grid) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(C::NUM_THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = &cluster_attr;
+    cfg.numAttrs = 1;
+    return cfg;
+  };
   // Per-device set-up of this variant (shared-memory attribute, resident CTAs
   // per wave), once per device; thread-safe.
   static std::mutex init_mu;
@@ -275,22 +293,33 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
         return ATTN_ERR_CUDA;
       if (occ < 1) return ATTN_ERR_RESOURCE;
       slots = sms * occ;
+      if constexpr (PAIR) {
+        // Resident pairs (both CTAs of a cluster on one GPC at once).
+        int clusters = 0;
+        const cudaLaunchConfig_t cfg = launch_cfg(static_cast<unsigned>(2 * sms));
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess)
+          return ATTN_ERR_CUDA;
+        if (clusters < 1) return ATTN_ERR_RESOURCE;
+        slots = clusters * C::CTAS;
+      }
       if (dev < 64) slots_of[dev].store(slots, std::memory_order_release);
     }
   }
-  const long long qt = (S + C::BM - 1) / C::BM;
+  // Units: BM rows of one (batch, head) per CTA, or 2 * BM per CTA pair (one
+  // unit per cluster; pairs take no key split).
+  const long long qt = (S + C::BM * C::CTAS - 1) / (C::BM * C::CTAS);
   const int n_kv = (S + BN - 1) / BN;
-  SplitPlan plan = plan_split(BH * qt, n_kv, slots, o.split);
+  SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, PAIR ? 1 : o.split);
   plan_workspace(&plan, C::BM, D, NQ, sizeof(float));
   if (o.plan_out) *o.plan_out = plan;
   if (o.plan_only) return ATTN_OK;
-  if (plan.ctas > INT_MAX || qt > INT_MAX) return ATTN_ERR_INVALID_ARG;
+  if (plan.ctas * C::CTAS > INT_MAX || qt > INT_MAX) return ATTN_ERR_INVALID_ARG;
 
   CUtensorMap mq, mk, mv, mo;
   int rc;
   const int bhi = static_cast<int>(BH);
   if ((rc = get_tensor_map(&mq, Q, dtype, D, S, bhi, q_rows, C::QROWS, o.cache_maps))) return rc;
-  if ((rc = get_tensor_map(&mk, K, dtype, D, S, bhi, kv_rows, BN, o.cache_maps))) return rc;
+  if ((rc = get_tensor_map(&mk, K, dtype, D, S, bhi, kv_rows, C::K_ROWS, o.cache_maps))) return rc;
   if ((rc = get_tensor_map(&mv, V, dtype, D, S, bhi, kv_rows, BN, o.cache_maps))) return rc;
   if ((rc = get_tensor_map(&mo, O, dtype, D, S, bhi, q_rows, C::QROWS, o.cache_maps))) return rc;
 
@@ -329,9 +358,14 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
     if (cudaMemsetAsync(p.ws_cnt, 0, plan.cnt_bytes, stream) != cudaSuccess) rc = ATTN_ERR_CUDA;
   }
   if (rc == ATTN_OK) {
-    kern<<<static_cast<unsigned>(plan.ctas), C::NUM_THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv,
-                                                                                     mo, p);
-    if (cudaGetLastError() != cudaSuccess) rc = ATTN_ERR_CUDA;
+    if constexpr (PAIR) {
+      const cudaLaunchConfig_t cfg = launch_cfg(static_cast<unsigned>(plan.ctas * C::CTAS));
+      if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mo, p) != cudaSuccess) rc = ATTN_ERR_CUDA;
+    } else {
+      kern<<<static_cast<unsigned>(plan.ctas), C::NUM_THREADS, C::SMEM_BYTES, stream>>>(mq, mk,
+                                                                                       mv, mo, p);
+      if (cudaGetLastError() != cudaSuccess) rc = ATTN_ERR_CUDA;
+    }
   }
   if (pooled && cudaFreeAsync(ws, stream) != cudaSuccess && rc == ATTN_OK) rc = ATTN_ERR_CUDA;
   return rc;

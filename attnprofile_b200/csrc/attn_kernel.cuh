@@ -70,11 +70,18 @@ enum : int {
 // 1 the wait for the last P V, 2 the partial-O write of a split part,
 // 3 its count-in, 4 the merge (split) or the O normalisation into shared
 // memory (whole unit), 5 the TMA store issue.
-constexpr int kProfPhases = 11;
+// Three trace phases relate the Q tiles of a two-tile CTA: 11 SOFTMAX of
+// tile 1 (its S observed -> its last P part signalled), 12 and 13 the MMA
+// issuer's window for tile 0 / tile 1 (first P part observed -> the tile's
+// next S issued, or its last P V committed); 14 the first P part signalled
+// by tile 0 (begin) and by tile 1 (end); 15 the MMA issuer's wait for V_j
+// (wait entered -> V_j observed landed); 16 its wait for K_{j+1}.
+constexpr int kProfPhases = 17;
 constexpr int kProfSlots = 32;
 enum : int {
   kPhLoadQ = 0, kPhLoadK = 1, kPhLoadV = 2, kPhQK = 3, kPhSoftmax = 4, kPhPV = 5,
-  kPhSmLoadS = 6, kPhSmMax = 7, kPhSmExp = 8, kPhSmStoreP = 9, kPhEpilogue = 10
+  kPhSmLoadS = 6, kPhSmMax = 7, kPhSmExp = 8, kPhSmStoreP = 9, kPhEpilogue = 10,
+  kPhSoftmaxT1 = 11, kPhMmaT0 = 12, kPhMmaT1 = 13, kPhPFirst = 14, kPhVWait = 15, kPhKWait = 16
 };
 enum : int {
   kEpAll = 0, kEpWaitO = 1, kEpPartial = 2, kEpCount = 3, kEpMerge = 4, kEpStore = 5
@@ -106,14 +113,18 @@ constexpr int kMaxSplit = 4;
 
 // What one CTA computes: BM query rows of one (batch, head) against key tiles
 // [kv_lo, kv_lo + n); part < 0 for a whole unit, else its slot in the workspace.
+// For CTA pairs a unit is the 2 * BM rows of one pair; `rank` is the CTA's
+// place in its pair (its rows start BM * rank into the unit), 0 otherwise.
 struct WorkTile {
-  int bh, q_row0, kv_lo, n, part;
+  int bh, q_row0, kv_lo, n, part, rank;
   long long slot;  // (split unit index) * split + part, for partial units
 };
 
-__device__ __forceinline__ WorkTile work_tile_of(int cta, int BM, const AttnParams& p) {
+__device__ __forceinline__ WorkTile work_tile_of(int cta, int BM, int ctas, int rank,
+                                                 const AttnParams& p) {
   WorkTile t;
   int u;
+  cta /= ctas;
   if (cta < p.num_whole) {
     u = cta;
     t.part = -1;
@@ -129,7 +140,8 @@ __device__ __forceinline__ WorkTile work_tile_of(int cta, int BM, const AttnPara
     t.slot = static_cast<long long>(r);
   }
   t.bh = u / p.qt_per_bh;
-  t.q_row0 = (u % p.qt_per_bh) * BM;
+  t.q_row0 = (u % p.qt_per_bh) * BM * ctas + rank * BM;
+  t.rank = rank;
   return t;
 }
 
@@ -163,18 +175,37 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
 #endif
 constexpr int kPolyPairsOf8 = ATTNPROF_POLY_PAIRS_OF_8;
 
-template <typename T, int D_, int BN_, int NQ_, int STAGES_>
+// Where the first published part of P ends, in quarters of the key tile
+// (2 = half: P V starts on the first BN/2 keys while the softmax computes the
+// rest).
+#ifndef ATTNPROF_PSPLIT_QUARTERS
+#define ATTNPROF_PSPLIT_QUARTERS 2
+#endif
+constexpr int kPsplitQuarters = ATTNPROF_PSPLIT_QUARTERS;
+
+
+// PAIR: the CTA is one of a cluster pair that shares every K/V tile through
+// cta_group::2 MMAs of M = 256 (tile i of the even CTA on rows 0-127, tile i
+// of the odd CTA on rows 128-255).  Each CTA loads half of every K tile (BN/2
+// keys) and half of every V tile (D/2 columns), so the per-SM shared-memory
+// traffic of the B operands, the TMA writes and the L2 reads halve and the
+// same ring holds twice as many key tiles.  The even CTA issues all MMAs.
+template <typename T, int D_, int BN_, int NQ_, int STAGES_, bool PAIR_ = false>
 struct AttnConfig {
   static constexpr int D = D_;
   static constexpr int BN = BN_;
   static constexpr int NQ = NQ_;
   static constexpr int STAGES = STAGES_;
+  static constexpr bool PAIR = PAIR_;
+  static constexpr int CTAS = PAIR ? 2 : 1;  // CTAs that share one MMA
   static constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
 
   static_assert(D == 64 || D == 128, "head dim must be 64 or 128");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
   static_assert(NQ == 1 || NQ == 2, "NQ must be 1 or 2");
   static_assert(STAGES >= 2, "need at least two K/V slots");
+  static_assert(!PAIR || (D == 128 && BN == 128 && NQ == 2),
+                "CTA pairs are built for D = 128, BN = 128, two Q tiles per CTA");
 
   static constexpr int QROWS = 128;  // rows per Q tile = MMA M = TMEM lanes
   static constexpr int BM = QROWS * NQ;
@@ -195,7 +226,14 @@ struct AttnConfig {
   // Shared memory (offsets from a 1024-byte aligned base).
   static constexpr int Q_TILE_BYTES = QROWS * D * 2;
   static constexpr int Q_BLK_BYTES = QROWS * 128;
-  static constexpr int KV_TILE_BYTES = BN * D * 2;
+  // One ring slot: a K or a V tile (this CTA's half of it for pairs).  K
+  // slots hold BN / CTAS keys as DBLK 64-column blocks of K_BLK_BYTES; V slots
+  // hold all BN keys of D / CTAS columns, 64-column blocks V_BLK_BYTES apart.
+  static constexpr int KV_TILE_BYTES = BN * D * 2 / CTAS;
+  static constexpr int K_ROWS = BN / CTAS;
+  static constexpr int K_BLK_BYTES = K_ROWS * 128;
+  static constexpr int V_BLK_BYTES = BN * 128;
+  static constexpr int V_DBLK = DBLK / CTAS;
   static constexpr int KV_BLK_BYTES = BN * 128;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + NQ * Q_TILE_BYTES;
@@ -214,7 +252,8 @@ struct AttnConfig {
   // piece (C3 at 256 x 96: 631 -> 664 TFLOP/s).  At D = 128 neither helps.
   static constexpr bool EXP_BOUND = NQ == 2 && D == 64 && NQ * (2 * BN + D) <= 512;
   static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND) ? 2 : 1;
-  static constexpr int PSPLIT_CHUNKS = BN / 64;
+  static constexpr int PSPLIT_CHUNKS =
+      (BN / 32) * kPsplitQuarters / 4 >= 1 ? (BN / 32) * kPsplitQuarters / 4 : 1;
   static constexpr int BAR_P_READY = BAR_S_FULL + NQ * NSBUF;      // [NQ][NSBUF][PHALVES]
   static constexpr int BAR_O_DONE = BAR_P_READY + NQ * NSBUF * PHALVES;  // every P V of tile i
   static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
@@ -254,8 +293,11 @@ struct AttnConfig {
                 "register split exceeds the launch allocation");
 
   static constexpr int POLY8 = kPolyPairsOf8 >= 0 ? kPolyPairsOf8 : (EXP_BOUND ? 2 : 0);
-  static constexpr uint32_t IDESC_S = ptx::idesc_f16(128, BN, kBF16, false);
-  static constexpr uint32_t IDESC_PV = ptx::idesc_f16(128, D, kBF16, true);
+  static constexpr int MMA_M = 128 * CTAS;
+  static constexpr uint32_t IDESC_S = ptx::idesc_f16(MMA_M, BN, kBF16, false);
+  static constexpr uint32_t IDESC_PV = ptx::idesc_f16(MMA_M, D, kBF16, true);
+  // Arrivals per P part: one per softmax warp, of both CTAs for pairs.
+  static constexpr int P_ARRIVALS = 4 * CTAS;
 };
 
 // Lazy-rescale threshold in log2 units: O and the row sum are rescaled only
@@ -320,6 +362,9 @@ static __device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t pari
 }
 
 // Bounded wait for the completion of the mbarrier phase with parity `parity`.
+// Also for the barriers that the peer CTA of a pair arrives on: the waits
+// keep the default (CTA-scope) acquire, like the arrivals; an acquire at
+// cluster scope on every poll made the pair kernel 27 % slower on B200.
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const WaitCtx& w,
                                          int site) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
@@ -379,10 +424,20 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
     prof.stamp(is_k ? kPhLoadK : kPhLoadV, j, 0);
     ptx::mbar_arrive_expect_tx(bar(C::BAR_KV_FULL + s), C::KV_TILE_BYTES);
     const uint32_t dst = sbase + C::OFF_KV + s * C::KV_TILE_BYTES;
+    const int key0 = (wt.kv_lo + j) * C::BN;
+    if (is_k) {
+      // K: keys [key0 + rank * K_ROWS, + K_ROWS), all D columns.
 #pragma unroll
-    for (int d = 0; d < C::DBLK; ++d)
-      ptx::tma_load_3d_hint(dst + d * C::KV_BLK_BYTES, is_k ? tmK : tmV, bar(C::BAR_KV_FULL + s),
-                            d * 64, (wt.kv_lo + j) * C::BN, bh, pol_kv);
+      for (int d = 0; d < C::DBLK; ++d)
+        ptx::tma_load_3d_hint(dst + d * C::K_BLK_BYTES, tmK, bar(C::BAR_KV_FULL + s), d * 64,
+                              key0 + wt.rank * C::K_ROWS, bh, pol_kv);
+    } else {
+      // V: all BN keys, column blocks [rank * V_DBLK, + V_DBLK).
+#pragma unroll
+      for (int d = 0; d < C::V_DBLK; ++d)
+        ptx::tma_load_3d_hint(dst + d * C::V_BLK_BYTES, tmV, bar(C::BAR_KV_FULL + s),
+                              (wt.rank * C::V_DBLK + d) * 64, key0, bh, pol_kv);
+    }
     last_issued[s] = t;
     ++t;
   };
@@ -413,8 +468,18 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
 template <class C, bool PROFILE>
 __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, const AttnParams& p,
                          const WaitCtx& w, const Prof<PROFILE>& prof, int i0, int i1) {
-  // Issues the MMAs of Q tiles [i0, i1) of this CTA.
+  // Issues the MMAs of Q tiles [i0, i1) of this CTA (for a CTA pair: of both
+  // CTAs, from the even one).
+  constexpr int G = C::CTAS;
   auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  // Completion signals that the softmax / producer warps wait on: in both
+  // CTAs of a pair.
+  auto signal = [&](uint32_t b) {
+    if constexpr (C::PAIR)
+      ptx::mma_commit_pair(b);
+    else
+      ptx::mma_commit(b);
+  };
   const int n = wt.n;
   bool ok = true;
 
@@ -425,7 +490,8 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
   // Wait for ring item t (K_j when is_k, else V_j) to land in its slot.
   auto ring_wait = [&](int& stage, bool is_k, int j) -> bool {
     stage = t % C::STAGES;
-    const bool r = wait_bar(bar(C::BAR_KV_FULL + stage), (t / C::STAGES) & 1, w, kSiteKvFull);
+    const bool r =
+        wait_bar(bar(C::BAR_KV_FULL + stage), (t / C::STAGES) & 1, w, kSiteKvFull);
     ++t;
     if (r) {
       if (i0 == 0) prof.stamp(is_k ? kPhLoadK : kPhLoadV, j, 1);
@@ -444,7 +510,7 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
   for (int i = 0; i < C::NQ; ++i)
     qd0[i] = ptx::smem_desc_sw128(sbase + C::OFF_Q + i * C::Q_TILE_BYTES, 16, 1024);
   const uint64_t kd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, 16, 1024);
-  const uint64_t vd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, C::KV_BLK_BYTES, 1024);
+  const uint64_t vd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, C::V_BLK_BYTES, 1024);
   auto slot_off = [](int stage) -> uint64_t {
     return static_cast<uint64_t>((stage * C::KV_TILE_BYTES) >> 4);
   };
@@ -457,8 +523,8 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
 #pragma unroll
     for (int kk = 0; kk < KSTEPS_S; ++kk) {
       const uint64_t qo = static_cast<uint64_t>(((kk >> 2) * C::Q_BLK_BYTES + (kk & 3) * 32) >> 4);
-      const uint64_t ko = static_cast<uint64_t>(((kk >> 2) * C::KV_BLK_BYTES + (kk & 3) * 32) >> 4);
-      ptx::mma_ss(d_tmem, qd0[i] + qo, kd + ko, C::IDESC_S, kk > 0 ? 1u : 0u);
+      const uint64_t ko = static_cast<uint64_t>(((kk >> 2) * C::K_BLK_BYTES + (kk & 3) * 32) >> 4);
+      ptx::mma_ss<G>(d_tmem, qd0[i] + qo, kd + ko, C::IDESC_S, kk > 0 ? 1u : 0u);
     }
   };
   // O_i += P_i(j) V_j : BN/16 MMAs of 128 x D x 16, A = P from TMEM; K-step
@@ -469,7 +535,7 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
     const uint64_t vd = vd0 + slot_off(stage);
 #pragma unroll
     for (int kk = k0; kk < k1; ++kk)
-      ptx::mma_ts(o_tmem, p_tmem + kk * 8, vd + static_cast<uint64_t>(kk * 2048 >> 4),
+      ptx::mma_ts<G>(o_tmem, p_tmem + kk * 8, vd + static_cast<uint64_t>(kk * 2048 >> 4),
                   C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
   };
 
@@ -480,14 +546,16 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
     for (int i = i0; i < i1; ++i) {
       if (i == 0) prof.stamp(kPhQK, jj, 0);
       issue_s(i, jj, sk);
-      ptx::mma_commit(bar(C::BAR_S_FULL + i * C::NSBUF + jj % C::NSBUF));
+      signal(bar(C::BAR_S_FULL + i * C::NSBUF + jj % C::NSBUF));
     }
-    ptx::mma_commit(bar(C::BAR_KV_EMPTY + sk));
+    signal(bar(C::BAR_KV_EMPTY + sk));
   }
 
   for (int j = 0; j < n && ok; ++j) {
     int sv;
+    if (i0 == 0) prof.stamp(kPhVWait, j, 0);
     if (!(ok = ring_wait(sv, false, j))) break;
+    if (i0 == 0) prof.stamp(kPhVWait, j, 1);
     const int jn = j + C::NSBUF;
     int sk = -1;
     for (int i = i0; i < i1 && ok; ++i) {
@@ -497,33 +565,79 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
       for (int h = 0; h < C::PHALVES; ++h) {
         if (!(ok = wait_bar(bar(pb + h), (j / C::NSBUF) & 1, w, kSitePReady))) break;
         ptx::tc_fence_after();
-        if (i == 0 && h == 0) prof.stamp(kPhPV, j, 0);
+        if (h == 0) {
+          if (i == 0) prof.stamp(kPhPV, j, 0);
+          prof.stamp(kPhMmaT0 + i, j, 0);
+        }
         constexpr int KSPLIT = C::PHALVES == 2 ? 2 * C::PSPLIT_CHUNKS : KSTEPS;
         issue_pv(i, j, sv, h == 0 ? 0 : KSPLIT, h == 0 ? KSPLIT : KSTEPS);
       }
       if (!ok) break;
-      ptx::mma_commit(bar(C::BAR_O_DONE + i));
-      if (j == n - 1) ptx::mma_commit(bar(C::BAR_O_FINAL + i));
+      signal(bar(C::BAR_O_DONE + i));
+      if (j == n - 1) signal(bar(C::BAR_O_FINAL + i));
       if (jn < n) {
-        if (sk < 0 && !(ok = ring_wait(sk, true, jn))) break;
+        if (sk < 0) {
+          if (i0 == 0) prof.stamp(kPhKWait, j, 0);
+          if (!(ok = ring_wait(sk, true, jn))) break;
+          if (i0 == 0) prof.stamp(kPhKWait, j, 1);
+        }
         if (i == 0) prof.stamp(kPhQK, jn, 0);
         issue_s(i, jn, sk);
-        ptx::mma_commit(bar(C::BAR_S_FULL + i * C::NSBUF + jn % C::NSBUF));
+        signal(bar(C::BAR_S_FULL + i * C::NSBUF + jn % C::NSBUF));
       }
+      prof.stamp(kPhMmaT0 + i, j, 1);
     }
     if (!ok) break;
-    ptx::mma_commit(bar(C::BAR_KV_EMPTY + sv));
-    if (sk >= 0) ptx::mma_commit(bar(C::BAR_KV_EMPTY + sk));
+    signal(bar(C::BAR_KV_EMPTY + sv));
+    if (sk >= 0) signal(bar(C::BAR_KV_EMPTY + sk));
   }
 
   // Drain: every MMA this thread issued has completed before TMEM is freed.
-  ptx::mma_commit(bar(C::BAR_DRAIN));
+  ptx::mma_commit<G>(bar(C::BAR_DRAIN));
   const unsigned long long t0 = ptx::globaltimer_ns();
   while (!ptx::mbar_try_wait(bar(C::BAR_DRAIN), 0)) {
     if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
       if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + kSiteDrain);
       break;
     }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Relay (odd CTA of a pair, one thread): the even CTA's MMAs read this CTA's
+// Q and K/V halves, so each landing of a load here (observed on this CTA's own
+// barrier, which the TMA completes) is passed on as an arrival on the even
+// CTA's barrier of the same slot; there the MMA issuer waits for both halves
+// (two arrivals).  Items in the producer's order: Q tiles, K_0, then V_j,
+// K_{j+1}.  A failed wait ends the relay; the even CTA then times out too.
+// ----------------------------------------------------------------------------
+template <class C>
+__device__ void relay_role(uint32_t sbase, const WorkTile& wt, const WaitCtx& w) {
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  // Waits with a suspend hint: the relay thread sleeps inside try_wait until
+  // the load lands instead of taking issue slots from the softmax warps of its
+  // SM sub-partition.
+  auto wait = [&](uint32_t b, uint32_t parity, int site) {
+    const unsigned long long t0 = ptx::globaltimer_ns();
+    while (!ptx::mbar_try_wait_sleep(b, parity, 20000u)) {
+      if (*w.abort) return false;
+      if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
+        *w.abort = 1;
+        if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + site);
+        return false;
+      }
+    }
+    return true;
+  };
+  for (int i = 0; i < C::NQ; ++i) {
+    if (!wait(bar(C::BAR_Q + i), 0, kSiteQ)) return;
+    ptx::mbar_arrive_cluster(ptx::mapa_shared(bar(C::BAR_Q + i), 0));
+  }
+  const int items = 2 * wt.n;
+  for (int t = 0; t < items; ++t) {
+    const int s = t % C::STAGES;
+    if (!wait(bar(C::BAR_KV_FULL + s), (t / C::STAGES) & 1, kSiteKvFull)) return;
+    ptx::mbar_arrive_cluster(ptx::mapa_shared(bar(C::BAR_KV_FULL + s), 0));
   }
 }
 
@@ -544,6 +658,17 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
   const int n = wt.n;
   const float sl2 = p.scale_log2;
   const bool rec = PROFILE && qi == 0 && wi == 0 && lane == 0;
+  const bool rec1 = PROFILE && qi == 1 && wi == 0 && lane == 0;
+  // P parts are signalled to the MMA issuer, in the even CTA of a pair.
+  auto p_arrive = [&](uint32_t b) {
+    if constexpr (C::PAIR) {
+      if (wt.rank != 0) {
+        ptx::mbar_arrive_cluster(ptx::mapa_shared(b, 0));
+        return;
+      }
+    }
+    ptx::mbar_arrive(b);
+  };
 
   float m_run = -INFINITY;  // running max (raw score units)
   float l_run = 0.f;        // running row sum of P (relative to m_run)
@@ -562,6 +687,7 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       prof.stamp(kPhSoftmax, j, 0);
       prof.stamp(kPhSmLoadS, j, 0);
     }
+    if (rec1) prof.stamp(kPhSoftmaxT1, j, 0);
 
     const int lim = p.S - (wt.kv_lo + j) * C::BN;  // valid key columns in this tile
     const int pbar = C::BAR_P_READY + (qi * C::NSBUF + buf) * C::PHALVES;
@@ -615,7 +741,8 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
     }
     if (__any_sync(0xffffffffu, resc)) {
       // O holds the sum through PV(j-1); wait for that MMA, then scale in place.
-      ok = __all_sync(0xffffffffu, wait_bar(bar(C::BAR_O_DONE + qi), (j - 1) & 1, w, kSiteODone));
+      ok = __all_sync(0xffffffffu,
+                      wait_bar(bar(C::BAR_O_DONE + qi), (j - 1) & 1, w, kSiteODone));
       if (!ok) break;
       ptx::tc_fence_after();
 #pragma unroll 1
@@ -678,7 +805,9 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar(pbar));
+        if (lane == 0) p_arrive(bar(pbar));
+        if (rec) prof.stamp(kPhPFirst, j, 0);
+        if (rec1) prof.stamp(kPhPFirst, j, 1);
       }
     }
     float sa, sb, sc_, sd;
@@ -693,8 +822,9 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
     if (rec) prof.stamp(kPhSmStoreP, j, 1);
     ptx::tc_fence_before();
     __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(bar(pbar + C::PHALVES - 1));
+    if (lane == 0) p_arrive(bar(pbar + C::PHALVES - 1));
     if (rec) prof.stamp(kPhSoftmax, j, 1);
+    if (rec1) prof.stamp(kPhSoftmaxT1, j, 1);
     l_run = l_run * alpha + sum;
   }
 
@@ -906,9 +1036,9 @@ __device__ void observer_role(uint32_t sbase, int n, const WaitCtx& w, const Pro
   }
 }
 
-template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE>
-__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
-                                  AttnConfig<T, D, BN, NQ, STAGES>::MIN_CTAS_PER_SM)
+template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE, bool PAIR = false>
+__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_THREADS,
+                                  AttnConfig<T, D, BN, NQ, STAGES, PAIR>::MIN_CTAS_PER_SM)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV,
@@ -918,28 +1048,35 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
 // generic compute_100 PTX (nvcc -arch=sm_100a does) gets an empty kernel there,
 // which a B200 never runs because the sm_100a binary matches it.
 #if defined(__CUDA_ARCH_FEAT_SM100_ALL) || !defined(__CUDA_ARCH__)
-  using C = AttnConfig<T, D, BN, NQ, STAGES>;
+  using C = AttnConfig<T, D, BN, NQ, STAGES, PAIR>;
+  constexpr int G = C::CTAS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = ptx::smem_u32(smem_raw);
   const uint32_t sbase = (raw_s + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - raw_s);
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const WorkTile wt = work_tile_of(blockIdx.x, C::BM, p);
+  // A pair is a cluster of two consecutive CTAs; every shared-memory offset
+  // below is the same in both (same kernel, same dynamic shared memory).
+  const int rank = PAIR ? static_cast<int>(ptx::cluster_ctarank()) : 0;
+  const WorkTile wt = work_tile_of(blockIdx.x, C::BM, G, rank, p);
 
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + C::OFF_MISC + 4);
 
   if (threadIdx.x == 0) {
     auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
-    for (int i = 0; i < C::NQ; ++i) ptx::mbar_init(bar(C::BAR_Q + i), 1);
+    // Load barriers of the even CTA of a pair also take the relay's arrival
+    // for the peer's half.
+    const uint32_t loads = (PAIR && rank == 0) ? 2u : 1u;
+    for (int i = 0; i < C::NQ; ++i) ptx::mbar_init(bar(C::BAR_Q + i), loads);
     for (int s = 0; s < C::STAGES; ++s) {
-      ptx::mbar_init(bar(C::BAR_KV_FULL + s), 1);
+      ptx::mbar_init(bar(C::BAR_KV_FULL + s), loads);
       ptx::mbar_init(bar(C::BAR_KV_EMPTY + s), C::NUM_ISSUERS);
     }
     for (int i = 0; i < C::NQ * C::NSBUF; ++i) ptx::mbar_init(bar(C::BAR_S_FULL + i), 1);
     for (int i = 0; i < C::NQ * C::NSBUF * C::PHALVES; ++i)
-      ptx::mbar_init(bar(C::BAR_P_READY + i), 4);
+      ptx::mbar_init(bar(C::BAR_P_READY + i), C::P_ARRIVALS);
     for (int i = 0; i < C::NQ; ++i) {
       ptx::mbar_init(bar(C::BAR_O_DONE + i), 1);
       ptx::mbar_init(bar(C::BAR_O_FINAL + i), 1);
@@ -955,11 +1092,13 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
     ptx::tma_prefetch_desc(&tmO);
   }
   if (warp == C::MMA_WARP) {
-    ptx::tmem_alloc(ptx::smem_u32(tmem_slot), C::TMEM_ALLOC);
-    ptx::tmem_relinquish();
+    ptx::tmem_alloc<G>(ptx::smem_u32(tmem_slot), C::TMEM_ALLOC);
+    ptx::tmem_relinquish<G>();
   }
   ptx::tc_fence_before();
   __syncthreads();
+  // Pairs: the peer's barriers are initialised before anything arrives on them.
+  if constexpr (PAIR) ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -974,9 +1113,13 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
     if (warp == C::LOAD_WARP) {
       if (lane == 0) load_role<C, PROFILE>(&tmQ, &tmK, &tmV, sbase, wt, p, w, prof);
     } else if (warp == C::MMA_WARP) {
-      if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, wt, p, w, prof, 0, C::NUM_ISSUERS == 2 ? 1 : C::NQ);
+      if (PAIR && rank != 0) {
+        if (lane == 0) relay_role<C>(sbase, wt, w);
+      } else if (lane == 0) {
+        mma_role<C, PROFILE>(tmem, sbase, wt, p, w, prof, 0, C::NUM_ISSUERS == 2 ? 1 : C::NQ);
+      }
     } else if (C::NUM_ISSUERS == 2 && warp == C::MMA_WARP2) {
-      if (lane == 0) mma_role<C, PROFILE>(tmem, sbase, wt, p, w, prof, 1, 2);
+      if (lane == 0 && (!PAIR || rank == 0)) mma_role<C, PROFILE>(tmem, sbase, wt, p, w, prof, 1, 2);
     } else if (warp == C::OBSERVER_WARP) {
       if constexpr (PROFILE) {
         if (lane == 0 && prof.buf != nullptr) observer_role<C>(sbase, wt.n, w, prof);
@@ -987,9 +1130,12 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES>::NUM_THREADS,
 
   ptx::tc_fence_before();
   __syncthreads();
+  // Pairs: neither CTA frees its tensor memory or exits while the even CTA's
+  // MMAs or the peer's arrivals may still reach it.
+  if constexpr (PAIR) ptx::cluster_sync();
   if (warp == C::MMA_WARP) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, C::TMEM_ALLOC);
+    ptx::tmem_dealloc<G>(tmem, C::TMEM_ALLOC);
   }
 #endif
 }

@@ -15,12 +15,16 @@ struct VariantInfo {
   int num_threads, smem_bytes, tmem_cols, stages;
 };
 
-template <typename T, int D, int BN, int NQ>
+template <typename T, int D, int BN, int NQ, bool PAIR = false>
 inline VariantInfo variant_info() {
-  constexpr int ST = auto_stages<T, D, BN, NQ>();
-  using C = AttnConfig<T, D, BN, NQ, ST>;
+  constexpr int ST = auto_stages<T, D, BN, NQ, PAIR>();
+  using C = AttnConfig<T, D, BN, NQ, ST, PAIR>;
   return VariantInfo{C::NUM_THREADS, C::SMEM_BYTES, C::TMEM_ALLOC, ST};
 }
+
+// BM = 512 (D = 128, BN = 128): a CTA pair of two 256-row CTAs sharing every
+// K/V tile through cta_group::2 MMAs (AttnConfig::PAIR).
+constexpr int kPairBM = 512;
 
 #define ATTNPROF_FOR_EACH_TILE(X) \
   X(128, 32)                      \
@@ -43,6 +47,11 @@ int dispatch_attn(int BM, int BN, const void* Q, const void* K, const void* V, v
         Q, K, V, O, B, H, S, q_rows, kv_rows, stream, o);
   ATTNPROF_FOR_EACH_TILE(ATTNPROF_CASE)
 #undef ATTNPROF_CASE
+  if constexpr (D == 128) {
+    if (BM == kPairBM && BN == 128)
+      return launch_attn<T, D, 128, 2, auto_stages<T, D, 128, 2, true>(), PROFILE, true>(
+          Q, K, V, O, B, H, S, q_rows, kv_rows, stream, o);
+  }
   return ATTN_ERR_UNSUPPORTED;
 }
 
@@ -55,6 +64,12 @@ int query_variant(int BM, int BN, VariantInfo* out) {
   }
   ATTNPROF_FOR_EACH_TILE(ATTNPROF_QCASE)
 #undef ATTNPROF_QCASE
+  if constexpr (D == 128) {
+    if (BM == kPairBM && BN == 128) {
+      *out = variant_info<T, D, 128, 2, true>();
+      return ATTN_OK;
+    }
+  }
   return ATTN_ERR_UNSUPPORTED;
 }
 

@@ -42,6 +42,11 @@ ALL_PHASES = PHASES + SUBPHASES
 # count-in of a split part, the merge (split) or O normalisation (whole), and
 # the TMA store issue.
 EPILOGUE_STEPS = ["epilogue", "ep-waitO", "ep-partial", "ep-count", "ep-merge", "ep-store"]
+# Trace phases (11-13) relating the two Q tiles of a BM = 256 CTA: SOFTMAX of
+# tile 1, and the MMA issuer's window per tile (first P part observed -> the
+# tile's next S issued).
+TRACE_PHASES = ["SOFTMAX-t1", "MMA-t0", "MMA-t1", "P-first", "V-wait", "K-wait"]
+TRACE_BASE = len(ALL_PHASES) + 1
 
 
 def summarize(stamps_list) -> dict:
@@ -76,10 +81,53 @@ def summarize(stamps_list) -> dict:
                 ep[n].append(int(e - b))
     for n, v in ep.items():
         out[n] = float(np.mean(v)) if v else float("nan")
+    tr = {n: [] for n in TRACE_PHASES}
+    for st in stamps_list:
+        a = np.asarray(st, dtype=np.int64)
+        for k, n in enumerate(TRACE_PHASES):
+            if a.shape[0] <= TRACE_BASE + k:
+                continue
+            b, e = a[TRACE_BASE + k, :, 0], a[TRACE_BASE + k, :, 1]
+            ok = (b != 0) & (e != 0) & (e >= b)
+            tr[n].extend((e[ok] - b[ok]).tolist())
+    for n, v in tr.items():
+        out[n] = float(np.mean(v)) if v else float("nan")
     return out
 
 
-def run(B=1, H=16, S=4096, D=128, BM=256, BN=128, dtype="f16", runs=20, cta=None, seed=0):
+def timeline(st, first: int = 8, count: int = 4) -> str:
+    """Event times of KV iterations [first, first + count) of one profiled CTA,
+    in cycles from the start of tile 0's SOFTMAX of iteration `first`:
+    each tile's SOFTMAX (S observed -> last P part signalled), the MMA
+    issuer's window per tile, and tile 0's P V completion as observed."""
+    import numpy as np
+    a = np.asarray(st, dtype=np.int64)
+    sm0 = PHASES.index("SOFTMAX")
+    pv0 = PHASES.index("GEMM-PV")
+    t0 = a[sm0, first, 0]
+    ex = len(PHASES) + SUBPHASES.index("exp")
+    qk = PHASES.index("GEMM-QK")
+    rows = ["| j | tile | SOFTMAX | exp step | first P part | MMA window (P seen -> next S "
+            "issued) | V_j wait | K_j+1 wait | S_j+1 issue | P V issue | P V done |",
+            "|---|---|---|---|---|---|---|---|---|---|---|"]
+    rel = lambda v: "-" if v == 0 else f"{int(v - t0)}"
+    tr = lambda k, j, w: a[TRACE_BASE + k, j, w] if a.shape[0] > TRACE_BASE + k else 0
+    for j in range(first, min(first + count, a.shape[1])):
+        rows.append(f"| {j} | 0 | {rel(a[sm0, j, 0])} .. {rel(a[sm0, j, 1])} | "
+                    f"{rel(a[ex, j, 0])} .. {rel(a[ex, j, 1])} | {rel(tr(3, j, 0))} | "
+                    f"{rel(tr(1, j, 0))} .. {rel(tr(1, j, 1))} | "
+                    f"{rel(tr(4, j, 0))} .. {rel(tr(4, j, 1))} | "
+                    f"{rel(tr(5, j, 0))} .. {rel(tr(5, j, 1))} | "
+                    f"{rel(a[qk, j + 1, 0]) if j + 1 < a.shape[1] else '-'} | "
+                    f"{rel(a[pv0, j, 0])} | {rel(a[pv0, j, 1])} |")
+        if tr(0, j, 0) != 0:
+            rows.append(f"| {j} | 1 | {rel(tr(0, j, 0))} .. {rel(tr(0, j, 1))} | | "
+                        f"{rel(tr(3, j, 1))} | {rel(tr(2, j, 0))} .. {rel(tr(2, j, 1))} | | | | | |")
+    return "\n".join(rows)
+
+
+def run(B=1, H=16, S=4096, D=128, BM=256, BN=128, dtype="f16", runs=20, cta=None, seed=0,
+        raw=False):
     import torch
     import attnprofile_b200 as ap
     dt = torch.float16 if dtype == "f16" else torch.bfloat16
@@ -97,16 +145,16 @@ def run(B=1, H=16, S=4096, D=128, BM=256, BN=128, dtype="f16", runs=20, cta=None
     rc, site = ap.get_status(torch.cuda.current_device())
     if rc != 0:
         raise RuntimeError(f"device status {site:#x}")
-    return summarize(stamps)
+    return stamps if raw else summarize(stamps)
 
 
 def table_header() -> str:
-    cols = ["BM", "BN"] + PHASES + ["period"] + SUBPHASES
+    cols = ["BM", "BN"] + PHASES + ["period"] + SUBPHASES + TRACE_PHASES
     return "| " + " | ".join(cols) + " |\n|" + "---|" * len(cols)
 
 
 def table_row(BM, BN, r) -> str:
-    vals = [f"{r[p]:.0f}" for p in PHASES + ["period"] + SUBPHASES]
+    vals = [f"{r[p]:.0f}" for p in PHASES + ["period"] + SUBPHASES + TRACE_PHASES]
     return f"| {BM} | {BN} | " + " | ".join(vals) + " |"
 
 
@@ -119,14 +167,19 @@ def main(argv=None):
     ap_.add_argument("--dtype", default="f16")
     ap_.add_argument("--tiles", default="256x128,128x128,256x64,128x64,128x256,256x32,128x32")
     ap_.add_argument("--runs", type=int, default=20)
+    ap_.add_argument("--timeline", type=int, default=0, metavar="N",
+                     help="also print N iterations (from 8) of one run's event timeline per tile")
     a = ap_.parse_args(argv)
     print(f"B={a.b} H={a.h} S={a.s} D={a.d} {a.dtype}: cycles (clock64) per phase, "
           f"mean over KV iterations 0-31 and {a.runs} runs")
     print(table_header())
     for t in a.tiles.split(","):
         bm, bn = (int(x) for x in t.split("x"))
-        r = run(a.b, a.h, a.s, a.d, bm, bn, a.dtype, a.runs)
-        print(table_row(bm, bn, r), flush=True)
+        st = run(a.b, a.h, a.s, a.d, bm, bn, a.dtype, a.runs, raw=True)
+        print(table_row(bm, bn, summarize(st)), flush=True)
+        if a.timeline:
+            print(f"\n{bm}x{bn} timeline (cycles, last run):\n" + timeline(st[-1], 8, a.timeline)
+                  + "\n", flush=True)
 
 
 if __name__ == "__main__":

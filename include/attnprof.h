@@ -45,7 +45,9 @@ extern "C" {
  * attn_fwd -- one attention forward over contiguous [B, H, S, D] tensors.
  * BM in {128, 256} query rows per CTA; BN in {32, 64, 96, 128, 256} keys per
  * KV tile (BM = 256 with BN = 256 does not fit tensor memory: UNSUPPORTED).
- * D in {64, 128}.  Asynchronous; returns launch errors only
+ * D in {64, 128}.  BM = 512 with BN = 128 at D = 128: a cluster of two
+ * 256-row CTAs sharing each K/V tile through cta_group::2 MMAs (no key
+ * split).  Asynchronous; returns launch errors only
  * (device-side timeouts are reported by attn_get_status).
  * Replaces: runAttn<...>(Q, K, V, O)            tuning/attn_test.cu:1665-1691
  *           (BM, BN as run-time values instead of template parameters).
@@ -73,8 +75,12 @@ int attn_fwd_padded(const void* Q, const void* K, const void* V, void* O, int B,
  * SOFTMAX, GEMM-PV (then the SOFTMAX steps S-load, max, exp, P-store) of its
  * first 32 KV iterations, and for its epilogue (phase 10; slots 0-5: the
  * whole epilogue, the wait for the last P V, partial-O write and count-in of
- * a split part, merge or O normalisation, O store issue), into
- * dev_profile_buf, laid out as u64 [11][32][2] (see attn_profile_layout).
+ * a split part, merge or O normalisation, O store issue), and trace phases
+ * relating the two Q tiles of BM = 256 (11 SOFTMAX of the second Q tile,
+ * 12 / 13 the MMA issuer's window per Q tile: first P part observed -> next S
+ * issued, 14 first P part signalled by tile 0 / tile 1, 15 / 16 the issuer's
+ * waits for V_j / K_{j+1}) into dev_profile_buf, laid out as u64 [17][32][2]
+ * (see attn_profile_layout).
  * The caller zeroes the buffer before the launch; unstamped slots stay 0.
  * Replaces: the clock64 profiler of attn.cu (ProfileResult attn.cu:5-22,
  *           stamps attn.cu:133-444, run_one_case attn.cu:1400-1494).
@@ -83,7 +89,7 @@ int attn_fwd_profiled(const void* Q, const void* K, const void* V, void* O, int 
                       int D, int dtype, int BM, int BN, void* stream,
                       unsigned long long* dev_profile_buf, int profile_cta);
 
-/* Profile buffer geometry: *phases = 11, *slots = 32 (u64 pairs). */
+/* Profile buffer geometry: *phases = 17, *slots = 32 (u64 pairs). */
 int attn_profile_layout(int* phases, int* slots);
 
 /*

@@ -106,6 +106,35 @@ def test_parity_ragged_tails(engine, oracle_mod, S, BM, BN):
     assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("B,H,S", [(1, 2, 512), (1, 3, 1024), (2, 3, 1000), (1, 1, 100),
+                                   (1, 5, 1536), (1, 2, 700), (1, 1, 1)])
+def test_parity_cta_pair(engine, oracle_mod, B, H, S, dt):
+    """BM = 512: two CTAs of a cluster share each K/V tile (cta_group::2
+    MMAs); pairs whose second CTA has no valid rows, ragged key tails."""
+    torch = _torch()
+    dtype = torch.float16 if dt == "f16" else torch.bfloat16
+    q, k, v = make_inputs(B, H, S, 128, dtype, seed=S * 3 + H)
+    out = run_gpu(engine, q, k, v, 512, 128)
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=128, dtype=code(dtype))
+    mx, mean = compare(oracle_mod, to_u16(out), ref, code(dtype))
+    assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
+
+
+def test_cta_pair_matches_single_cta(engine):
+    """At a size the oracle would take long on: the pair against the
+    single-CTA kernel (same softmax arithmetic; the tensor core's summation
+    order within an M = 256 MMA may differ in the last bit)."""
+    torch = _torch()
+    q, k, v = (x.cuda() for x in make_inputs(2, 8, 4096, 128, torch.float16, seed=5))
+    a = engine.attn(q, k, v, BM=256, BN=128)
+    b = engine.attn(q, k, v, BM=512, BN=128)
+    torch.cuda.synchronize()
+    assert engine.get_status(0)[0] == 0
+    d = (a.float() - b.float()).abs()
+    assert d.max().item() <= MAX_ABS and d.mean().item() <= MEAN_ABS / 10
+
+
 @pytest.mark.parametrize("path", GOLDEN, ids=lambda p: p.stem)
 def test_kernel_vs_reference_golden(engine, oracle_mod, path):
     """The kernel on the reference's own fixture inputs against the output the

@@ -55,7 +55,7 @@ def check_rows(engine, oracle_mod, B, H, S, D, dtype, sigma, BM, BN, rows_per_un
     assert np.isfinite(oracle_mod.to_f32(o[:: max(1, o.shape[0] // 4)], dt)).all()
 
 
-@pytest.mark.parametrize("BM,BN", [(256, 128), (128, 128), (128, 256), (256, 64)])
+@pytest.mark.parametrize("BM,BN", [(256, 128), (128, 128), (128, 256), (256, 64), (512, 128)])
 def test_c2_f16_d128(engine, oracle_mod, BM, BN):
     torch = _torch()
     check_rows(engine, oracle_mod, 1, 16, 4096, 128, torch.float16, 1.0, BM, BN, 24, 100)

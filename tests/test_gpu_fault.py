@@ -22,9 +22,11 @@ def test_bounded_wait_reports_timeout_and_context_survives(engine):
     try:
         engine.debug_fault(1)
         # one MMA issuer (NSBUF = 1), one issuer per Q tile (256 x 64, 256 x 32),
-        # and a key-split launch whose parts never count in
+        # a key-split launch whose parts never count in, and CTA pairs (the
+        # odd CTA's relay and the even CTA's issuer both time out; the two
+        # meet at the cluster barrier before freeing tensor memory)
         for bm, bn, split in ((128, 128, 0), (256, 128, 0), (256, 64, 0), (256, 32, 0),
-                              (256, 128, 2)):
+                              (256, 128, 2), (512, 128, 0)):
             engine.set_split(split)
             engine.attn(Q, K, V, BM=bm, BN=bn)
             rc, site = engine.get_status(0, reset=True)
@@ -35,7 +37,7 @@ def test_bounded_wait_reports_timeout_and_context_survives(engine):
         engine.set_split(0)
         engine.set_timeout_ns(2_000_000_000)
     ref = torch.softmax((Q.float() @ K.float().transpose(-1, -2)) / 128 ** 0.5, -1) @ V.float()
-    for bm, bn, split in ((256, 128, 0), (256, 64, 0), (256, 128, 2)):
+    for bm, bn, split in ((256, 128, 0), (256, 64, 0), (256, 128, 2), (512, 128, 0)):
         engine.set_split(split)
         try:
             O = engine.attn(Q, K, V, BM=bm, BN=bn)
