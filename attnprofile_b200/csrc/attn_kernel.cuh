@@ -265,7 +265,8 @@ struct AttnConfig {
   static constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for manual 1024 B alignment
 
   // Warp roles.
-  static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
+  static constexpr int WARPS_PER_TILE = 4;
+  static constexpr int NUM_SOFTMAX_WARPS = WARPS_PER_TILE * NQ;
   static constexpr int LOAD_WARP = NUM_SOFTMAX_WARPS;
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;
   static constexpr int OBSERVER_WARP = NUM_SOFTMAX_WARPS + 2;  // profiler only
@@ -284,20 +285,23 @@ struct AttnConfig {
   // One 128-row Q tile with narrow key tiles fits two CTAs per SM (shared
   // and tensor memory); the register budget is capped to keep that possible.
   static constexpr int MIN_CTAS_PER_SM = (NQ == 1 && BN <= 64) ? 2 : 1;
-  // Register split for NQ = 2 (384 threads launched at 168 registers each =
-  // 64512): softmax warpgroups 2 x 128 x 192 + producer/MMA warpgroup
-  // 128 x 120 = 64512.
+  // Register split for NQ = 2: 384 threads launched at 168 registers each
+  // (64512): softmax warpgroups 2 x 128 x 192 + producer/MMA warpgroup
+  // 128 x 120.
+  static constexpr int LAUNCH_REGS = (65536 / NUM_THREADS) & ~7;
   static constexpr uint32_t REG_SOFTMAX = 192;
   static constexpr uint32_t REG_OTHER = 120;
-  static_assert(NQ != 2 || 2 * 128 * REG_SOFTMAX + 128 * REG_OTHER <= 384 * 168,
+  static_assert(NQ != 2 || NUM_SOFTMAX_WARPS * 32 * REG_SOFTMAX + 128 * REG_OTHER <=
+                               NUM_THREADS * LAUNCH_REGS,
                 "register split exceeds the launch allocation");
 
   static constexpr int POLY8 = kPolyPairsOf8 >= 0 ? kPolyPairsOf8 : (EXP_BOUND ? 2 : 0);
   static constexpr int MMA_M = 128 * CTAS;
   static constexpr uint32_t IDESC_S = ptx::idesc_f16(MMA_M, BN, kBF16, false);
   static constexpr uint32_t IDESC_PV = ptx::idesc_f16(MMA_M, D, kBF16, true);
-  // Arrivals per P part: one per softmax warp, of both CTAs for pairs.
-  static constexpr int P_ARRIVALS = 4 * CTAS;
+  // Arrivals per P part: one per softmax warp of the tile, of both CTAs for
+  // pairs.
+  static constexpr int P_ARRIVALS = WARPS_PER_TILE * CTAS;
 };
 
 // Lazy-rescale threshold in log2 units: O and the row sum are rescaled only
@@ -563,6 +567,13 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
       constexpr int KSTEPS = C::BN / 16;
 #pragma unroll
       for (int h = 0; h < C::PHALVES; ++h) {
+        // K_{j+NSBUF} is normally resident long before the last P part: its
+        // wait sits here, off the path from that P part to the next S.
+        if (h == C::PHALVES - 1 && jn < n && sk < 0) {
+          if (i0 == 0) prof.stamp(kPhKWait, j, 0);
+          if (!(ok = ring_wait(sk, true, jn))) break;
+          if (i0 == 0) prof.stamp(kPhKWait, j, 1);
+        }
         if (!(ok = wait_bar(bar(pb + h), (j / C::NSBUF) & 1, w, kSitePReady))) break;
         ptx::tc_fence_after();
         if (h == 0) {
@@ -573,18 +584,16 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
         issue_pv(i, j, sv, h == 0 ? 0 : KSPLIT, h == 0 ? KSPLIT : KSTEPS);
       }
       if (!ok) break;
-      signal(bar(C::BAR_O_DONE + i));
-      if (j == n - 1) signal(bar(C::BAR_O_FINAL + i));
+      // The tile's next S follows its last P V MMAs directly; the O commits
+      // come after it (O_DONE then also covers that S, which every waiter on
+      // O_DONE has already seen complete).
       if (jn < n) {
-        if (sk < 0) {
-          if (i0 == 0) prof.stamp(kPhKWait, j, 0);
-          if (!(ok = ring_wait(sk, true, jn))) break;
-          if (i0 == 0) prof.stamp(kPhKWait, j, 1);
-        }
         if (i == 0) prof.stamp(kPhQK, jn, 0);
         issue_s(i, jn, sk);
         signal(bar(C::BAR_S_FULL + i * C::NSBUF + jn % C::NSBUF));
       }
+      signal(bar(C::BAR_O_DONE + i));
+      if (j == n - 1) signal(bar(C::BAR_O_FINAL + i));
       prof.stamp(kPhMmaT0 + i, j, 1);
     }
     if (!ok) break;

@@ -11,7 +11,8 @@ begin/end stamps per KV iteration (first 32 iterations, one slot each):
   LoadV    producer issues V_j (slot free)      -> MMA warp sees V_j landed
   GEMM-QK  MMA warp issues S_0 = Q_0 K_j^T       -> softmax warp sees S_0 complete
   SOFTMAX  softmax warp sees S_0                 -> P_0 written to TMEM and signalled
-  GEMM-PV  MMA warp issues O_0 += P_0 V_j        -> observer warp sees it complete
+  GEMM-PV  MMA warp issues O_0 += P_0 V_j        -> observer warp sees it (and the
+           next S_0, committed with it) complete
 
 (Tile 0 of the CTA; all stamps come from one SM's clock.)  SOFTMAX is also
 split into its steps: S-ld (tcgen05.ld of S and its wait), max (row max and
