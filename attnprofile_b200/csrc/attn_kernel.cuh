@@ -175,11 +175,12 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
 #endif
 constexpr int kPolyPairsOf8 = ATTNPROF_POLY_PAIRS_OF_8;
 
-// Where the first published part of P ends, in quarters of the key tile
-// (2 = half: P V starts on the first BN/2 keys while the softmax computes the
-// rest).
+// Where the first published part of P ends, in quarters of the key tile: P V
+// starts on those keys while the softmax computes the rest, and only the
+// rest's P V (with the next S) follows the last part.  -1 (default): 3 at
+// BN = 128 (C2: 1068 -> 1082 TFLOP/s against 2), 2 elsewhere.
 #ifndef ATTNPROF_PSPLIT_QUARTERS
-#define ATTNPROF_PSPLIT_QUARTERS 2
+#define ATTNPROF_PSPLIT_QUARTERS -1
 #endif
 constexpr int kPsplitQuarters = ATTNPROF_PSPLIT_QUARTERS;
 
@@ -252,8 +253,10 @@ struct AttnConfig {
   // piece (C3 at 256 x 96: 631 -> 664 TFLOP/s).  At D = 128 neither helps.
   static constexpr bool EXP_BOUND = NQ == 2 && D == 64 && NQ * (2 * BN + D) <= 512;
   static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND) ? 2 : 1;
+  static constexpr int PSPLIT_QUARTERS = kPsplitQuarters >= 0 ? kPsplitQuarters
+                                                              : (BN == 128 ? 3 : 2);
   static constexpr int PSPLIT_CHUNKS =
-      (BN / 32) * kPsplitQuarters / 4 >= 1 ? (BN / 32) * kPsplitQuarters / 4 : 1;
+      (BN / 32) * PSPLIT_QUARTERS / 4 >= 1 ? (BN / 32) * PSPLIT_QUARTERS / 4 : 1;
   static constexpr int BAR_P_READY = BAR_S_FULL + NQ * NSBUF;      // [NQ][NSBUF][PHALVES]
   static constexpr int BAR_O_DONE = BAR_P_READY + NQ * NSBUF * PHALVES;  // every P V of tile i
   static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
