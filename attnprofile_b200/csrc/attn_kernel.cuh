@@ -30,9 +30,16 @@
 // (NQ * (2 * BN + D) <= 512 columns) so Q K_{j+1}^T overlaps the softmax of
 // tile j; two-tile CTAs then issue each tile's MMAs from its own warp.
 //
+// CTA pairs (AttnConfig::PAIR, BM = 512 on the host): a cluster of two
+// two-tile CTAs whose tile i shares one cta_group::2 MMA of M = 256; each CTA
+// loads half of every K and V tile, the even CTA issues the MMAs and fans
+// its commits out to both, a relay thread in the odd CTA forwards the
+// landing of its loads to the even CTA's barriers.
+//
 // Every wait is bounded (see wait_bar): on expiry the kernel records an error
 // code in a device status word, raises a CTA-local abort flag so the other
-// roles stop waiting, drains its own outstanding tensor-core work and returns.
+// roles stop waiting, drains its own outstanding tensor-core work and returns
+// (a pair's two CTAs then meet at the final cluster barrier).
 #pragma once
 
 #include <cuda_bf16.h>
