@@ -16,12 +16,13 @@ def _setup():
     return torch, ([0, 1] if n >= 2 else [0, 0])
 
 
-def test_sharded_matches_single_call(engine):
+@pytest.mark.parametrize("BM", [256, 512])
+def test_sharded_matches_single_call(engine, BM):
     torch, devices = _setup()
     B, H, S, D = 2, 4, 512, 128
     g = torch.Generator().manual_seed(5)
     Q, K, V = (torch.randn(B, H, S, D, generator=g).half() for _ in range(3))
-    ref = engine.attn(Q.cuda(0), K.cuda(0), V.cuda(0)).cpu()
+    ref = engine.attn(Q.cuda(0), K.cuda(0), V.cuda(0), BM=BM).cpu()
     U = B * H
     shards = [engine.shard_range(U, len(devices), r) for r in range(len(devices))]
     flat = lambda t: t.reshape(1, U, S, D)
@@ -29,7 +30,7 @@ def test_sharded_matches_single_call(engine):
     Ks = [flat(K)[:, a:b].contiguous().cuda(d) for (a, b), d in zip(shards, devices)]
     Vs = [flat(V)[:, a:b].contiguous().cuda(d) for (a, b), d in zip(shards, devices)]
     Os = [torch.empty_like(q) for q in Qs]
-    ms = engine.attn_sharded(Qs, Ks, Vs, Os, devices, B=B, H=H)
+    ms = engine.attn_sharded(Qs, Ks, Vs, Os, devices, B=B, H=H, BM=BM)
     assert len(ms) == len(devices) and all(m > 0 for m in ms)
     got = torch.cat([o.cpu() for o in Os], dim=1).reshape(B, H, S, D)
     assert torch.equal(got, ref)
