@@ -177,10 +177,22 @@ def cpu_baseline_reference(wl):
         return None
     d = json.loads(line[-1])
     D = 128 if cfg == "c2head" else 64
-    return {"value": d["tflops"], "unit": "TFLOP/s", "cores": threads, "kind": "reference",
-            "sample": (f"{d['heads']} heads of 1x1x4096x{D} fp16 (one C2/C3 head per thread), "
-                       f"the reference's verify_attn host oracle (tuning/utils.cuh:139-198) "
-                       f"compiled from its sources; {d['seconds']:.2f} s wall")}
+    out = {"value": d["tflops"], "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+           "sample": (f"{d['heads']} heads of 1x1x4096x{D} fp16 (one C2/C3 head per thread), "
+                      f"the reference's verify_attn host oracle (tuning/utils.cuh:139-198) "
+                      f"compiled from its sources; {d['seconds']:.2f} s wall")}
+    # C1 (1x1x512x128), the reference's CPU-runnable case: one thread as the
+    # reference runs it, and one C1 problem per host thread at once.
+    c1 = {}
+    for key, t in (("gflops_1_thread", 1), ("gflops_all_threads", threads)):
+        r = subprocess.run([str(exe), "time", "c1", str(t)], capture_output=True, text=True,
+                           timeout=120)
+        ln = [x for x in r.stderr.splitlines() if x.startswith("{")]
+        if r.returncode == 0 and ln:
+            c1[key] = json.loads(ln[-1])["tflops"] * 1e3
+    if c1:
+        out["c1"] = dict(c1, threads=threads, shape="1x1x512x128 fp16")
+    return out
 
 
 # ---------------------------------------------------------------------------
