@@ -30,6 +30,11 @@
  * Parity pin: tests/golden holds outputs of the reference's own verify_attn
  * (compiled from its sources under a host shim, oracle/ref_shim.cu); this
  * restatement reproduces them bit for bit.
+ *
+ * oracle_attn_alt restates the reference's second CPU oracle (the root test
+ * driver verify_attn.cu:4619-4674), which computes the same function in
+ * another floating-point order; it is a cross-check of this file, not the
+ * parity target.
  */
 #include <float.h>
 #include <math.h>
@@ -150,6 +155,54 @@ static void attn_row(const uint16_t* q, const uint16_t* Kh, const uint16_t* Vh, 
   for (int d = 0; d < D; ++d) out[d] = from_f32(acc[d] * inv_sum, bf16);
 }
 
+/* The second CPU oracle of the reference, at the end of its root-level test
+ * driver (verify_attn.cu:4619-4674): the same online softmax over key tiles
+ * of BN, written in a different floating-point order --
+ *   alpha  = exp2f((m_prev - m_new) * scale)     (no first-tile special case:
+ *            m_prev = -FLT_MAX makes the argument huge and alpha 0)
+ *   p      = exp2f((score - m_new) * scale)      (subtract, then scale)
+ *   l      = l * alpha, then l += p one key at a time
+ *   O      = round(acc[d] / l)                   (a division, not 1/l times)
+ * P is still rounded to the storage type before PV and l uses the unrounded
+ * P.  Only the rounding of intermediate values differs from attn_row, so the
+ * two oracles agree to about one output ulp; the tests hold them to that. */
+static void attn_row_alt(const uint16_t* q, const uint16_t* Kh, const uint16_t* Vh,
+                         uint16_t* out, int S, int D, int bn_tile, int bf16, float* scores,
+                         float* acc, float* qf) {
+  const float scale = sqrtf(1.0f / (float)D) * 1.44269504f;   /* verify_attn.cu:4622 */
+  for (int d = 0; d < D; ++d) {
+    acc[d] = 0.0f;
+    qf[d] = to_f32(q[d], bf16);
+  }
+  float m_prev = -FLT_MAX;
+  float l_prev = 0.0f;
+  for (int ks0 = 0; ks0 < S; ks0 += bn_tile) {                 /* :4632 */
+    const int tile_n = ks0 + bn_tile <= S ? bn_tile : S - ks0;
+    float m_tile = -FLT_MAX;
+    for (int t = 0; t < tile_n; ++t) {                          /* :4636-4645 */
+      const uint16_t* k = Kh + (size_t)(ks0 + t) * D;
+      float score = 0.0f;
+      for (int d = 0; d < D; ++d) score += qf[d] * to_f32(k[d], bf16);
+      scores[t] = score;
+      m_tile = fmaxf(m_tile, score);
+    }
+    const float m_new = fmaxf(m_prev, m_tile);                  /* :4648-4649 */
+    const float alpha = exp2f((m_prev - m_new) * scale);
+    for (int d = 0; d < D; ++d) acc[d] *= alpha;                /* :4651-4653 */
+    float l_new = l_prev * alpha;                               /* :4655 */
+    for (int t = 0; t < tile_n; ++t) {                          /* :4656-4665 */
+      const float p = exp2f((scores[t] - m_new) * scale);
+      const float p_st = to_f32(from_f32(p, bf16), bf16);
+      l_new += p;
+      const uint16_t* v = Vh + (size_t)(ks0 + t) * D;
+      for (int d = 0; d < D; ++d) acc[d] += p_st * to_f32(v[d], bf16);
+    }
+    m_prev = m_new;
+    l_prev = l_new;
+  }
+  for (int d = 0; d < D; ++d) out[d] = from_f32(acc[d] / l_prev, bf16); /* :4671-4674 */
+}
+
 static int check_args(int B, int H, int S, int D, long sqo, long skv, int bn_tile, int dtype) {
   if (B < 0 || H < 0 || S < 0 || D <= 0 || bn_tile <= 0) return -1;
   if (sqo < S || skv < S) return -1;
@@ -193,6 +246,51 @@ int oracle_attn(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_
         const uint16_t* Vh = V + (size_t)u * skv * D;
         attn_row(Q + ((size_t)u * sqo + s) * D, Kh, Vh, O + ((size_t)u * sqo + s) * D, S, D,
                  bn_tile, dtype, scores, acc, qf);
+      }
+    }
+    free(scores);
+    free(acc);
+    free(qf);
+  }
+  (void)nthreads;
+  return err;
+}
+
+/*
+ * Full attention in the floating-point order of the reference's second CPU
+ * oracle (attn_row_alt).  Same arguments, threading and return codes as
+ * oracle_attn.
+ */
+int oracle_attn_alt(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int B,
+                    int H, int S, int D, long sqo, long skv, int bn_tile, int dtype,
+                    int nthreads) {
+  const int rc = check_args(B, H, S, D, sqo, skv, bn_tile, dtype);
+  if (rc) return rc;
+  const long total = (long)B * H * S;
+  int err = 0;
+#ifdef _OPENMP
+  const int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel num_threads(nt)
+#endif
+  {
+    float* scores = (float*)malloc(sizeof(float) * (size_t)(bn_tile));
+    float* acc = (float*)malloc(sizeof(float) * (size_t)D);
+    float* qf = (float*)malloc(sizeof(float) * (size_t)D);
+    if (!scores || !acc || !qf) {
+#ifdef _OPENMP
+#pragma omp atomic write
+#endif
+      err = -3;
+    } else {
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 16)
+#endif
+      for (long r = 0; r < total; ++r) {
+        const long u = r / S;
+        const long s = r % S;
+        attn_row_alt(Q + ((size_t)u * sqo + s) * D, K + (size_t)u * skv * D,
+                     V + (size_t)u * skv * D, O + ((size_t)u * sqo + s) * D, S, D, bn_tile,
+                     dtype, scores, acc, qf);
       }
     }
     free(scores);

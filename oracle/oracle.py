@@ -39,6 +39,8 @@ def lib() -> ctypes.CDLL:
                                   ctypes.c_int, ctypes.c_int, ctypes.c_long, ctypes.c_long,
                                   ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.oracle_attn.restype = ctypes.c_int
+        L.oracle_attn_alt.argtypes = L.oracle_attn.argtypes
+        L.oracle_attn_alt.restype = ctypes.c_int
         L.oracle_attn_rows.argtypes = [u16p, u16p, u16p, u16p, ctypes.POINTER(ctypes.c_int64),
                                        ctypes.c_long, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_long, ctypes.c_long, ctypes.c_int,
@@ -81,6 +83,35 @@ def attention(Q, K, V, *, S: int | None = None, bn_tile: int = 128, dtype: int =
     if rc != 0:
         raise ValueError(f"oracle_attn failed: {rc}")
     return out
+
+
+def attention_alt(Q, K, V, *, S: int | None = None, bn_tile: int = 128, dtype: int = F16,
+                  nthreads: int = 0) -> np.ndarray:
+    """attention() in the floating-point order of the reference's second CPU
+    oracle (verify_attn.cu:4619-4674): the same function, other roundings."""
+    q, k, v = _u16(Q), _u16(K), _u16(V)
+    B, H, sqo, D = q.shape
+    skv = k.shape[2]
+    S = sqo if S is None else S
+    out = np.zeros_like(q)
+    rc = lib().oracle_attn_alt(_ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, S, D, sqo, skv,
+                               bn_tile, dtype, nthreads)
+    if rc != 0:
+        raise ValueError(f"oracle_attn_alt failed: {rc}")
+    return out
+
+
+def pattern_inputs(B: int, H: int, S: int, D: int, dtype: int = F16):
+    """The deterministic inputs of the reference's root test driver
+    (verify_attn.cu:4575-4591): with i the flat [B, H, S, D] index,
+    q = ((13 i + 7) mod 31 - 15) / 128, k = ((17 i + 5) mod 29 - 14) / 128,
+    v = ((19 i + 3) mod 23 - 11) / 128, all exact in f16 and bf16."""
+    i = np.arange(B * H * S * D, dtype=np.int64)
+    q = ((i * 13 + 7) % 31 - 15).astype(np.float32) / 128.0
+    k = ((i * 17 + 5) % 29 - 14).astype(np.float32) / 128.0
+    v = ((i * 19 + 3) % 23 - 11).astype(np.float32) / 128.0
+    shape = (B, H, S, D)
+    return tuple(from_f32(a, dtype).reshape(shape) for a in (q, k, v))
 
 
 def attention_rows(Q, K, V, rows, *, S: int | None = None, bn_tile: int = 128,
