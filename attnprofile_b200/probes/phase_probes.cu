@@ -21,7 +21,14 @@
 // it and the program exits non-zero.  Operands are zero-filled or synthetic:
 // the probes measure time, not results.
 //
-// Usage: phase_probes [tma|mma|softmax|all]
+//   overlap  one Q tile's MMA sequence while two softmax warpgroups run on
+//            other tensor-memory columns and/or a TMA warp streams K tiles
+//            into shared memory, against each alone.
+//   issue    how fast one thread issues tcgen05.mma and how far it runs
+//            ahead of the tensor pipe (alone and beside softmax warps), and
+//            whether a second issuing thread raises the issue rate.
+//
+// Usage: phase_probes [tma|mma|softmax|overlap|issue|all]
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -313,6 +320,288 @@ __global__ void __launch_bounds__(128 * NWG, 1) softmax_probe(int iters, unsigne
   }
 }
 
+// ---------------------------------------------------------------------------
+// The softmax step of the softmax probe (tcgen05.ld of a 128-column S row,
+// row max, exp2 on MUFU, P packed to f16 and stored back with tcgen05.st),
+// for the probes that run it beside other work; returns the row sum.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void softmax_init(uint32_t lane_base, uint32_t s_col) {
+  uint32_t r[32];
+#pragma unroll
+  for (int c = 0; c < BN / 32; ++c) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      r[e] = __float_as_uint(0.37f * (((threadIdx.x * 131 + c * 32 + e) * 2654435761u >> 20) % 19) - 3.3f);
+    ptx::tmem_st32(lane_base + s_col + c * 32, r);
+  }
+  ptx::tmem_wait_st();
+}
+
+__device__ __forceinline__ float softmax_steps(uint32_t lane_base, uint32_t s_col, int iters) {
+  const float sl2 = 0.12752f;
+  float m_run = -INFINITY, l_run = 0.f;
+#pragma unroll 1
+  for (int it = 0; it < iters; ++it) {
+    uint32_t sv[BN];
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t(&r)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]);
+      ptx::tmem_ld32(lane_base + s_col + c * 32, r);
+    }
+    ptx::tmem_wait_ld();
+    ptx::reg_fence(sv);
+    const float m_new = row_max<BN>(sv, m_run);
+    const float alpha = ptx::ex2_approx((m_run - m_new) * sl2);
+    m_run = m_new;
+    const float neg = -m_new * sl2;
+    const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2), negx2 = ptx::f2_pack(neg, neg);
+    uint64_t part[2] = {0ull, 0ull};
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int c0 = c * 32 + 2 * e;
+        const uint64_t x2 = ptx::f2_fma(
+            ptx::f2_pack(__uint_as_float(sv[c0]), __uint_as_float(sv[c0 + 1])), sl2x2, negx2);
+        float x0, x1;
+        ptx::f2_unpack(x2, x0, x1);
+        const float p0 = ptx::ex2_approx(x0), p1 = ptx::ex2_approx(x1);
+        part[e & 1] = ptx::f2_add(part[e & 1], ptx::f2_pack(p0, p1));
+        __half2 h = __floats2half2_rn(p0, p1);
+        pk[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      ptx::tmem_st16(lane_base + s_col + c * 16, pk);
+    }
+    ptx::tmem_wait_st();
+    float a, b, c, d;
+    ptx::f2_unpack(part[0], a, b);
+    ptx::f2_unpack(part[1], c, d);
+    l_run = l_run * alpha + ((a + b) + (c + d));
+  }
+  return l_run;
+}
+
+// ---------------------------------------------------------------------------
+// overlap: one Q tile's MMA sequence (P V then S = Q K^T: 16 MMAs, 1024
+// cycles of tensor work per iteration; S in columns 0-127, O in 128-255) by
+// one issuing thread, while two softmax warpgroups run the softmax step on
+// columns 256-511 and/or a TMA warp streams K tiles into shared memory --
+// each alone and together, to see whether any of them slows the others.
+// ---------------------------------------------------------------------------
+constexpr int OVL_THREADS = 256 + 64;
+constexpr int OVL_RING = 3;  // K tiles streamed by TMA into slots after Q, K, V
+constexpr int OVL_SMEM = (3 + OVL_RING) * 32768 + 1024;  // one CTA per SM
+
+template <bool MMA_ON, bool SOFTMAX_ON, bool TMA_ON>
+__global__ void __launch_bounds__(OVL_THREADS, 1)
+    overlap_probe(const __grid_constant__ CUtensorMap tmK, int heads, int tma_tiles, int mma_iters,
+                  int sm_iters, unsigned long long* cycles, float* sink) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - ptx::smem_u32(smem_raw));
+  __shared__ uint32_t tmem_slot;
+  __shared__ __align__(8) uint64_t done, ring_full[OVL_RING];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 3 * 32768 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(g)[i] = 0;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(&done), 1);
+    for (int r = 0; r < OVL_RING; ++r) ptx::mbar_init(ptx::smem_u32(&ring_full[r]), 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_u32(&tmem_slot), 512);
+    ptx::tmem_relinquish();
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const int wg = warp / 4, wi = warp & 3;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(wi * 32) << 16);
+  const uint32_t s_col = 256 + wg * BN;
+  if (warp < 8) softmax_init(lane_base, s_col);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+
+  if (warp < 8 && SOFTMAX_ON) {
+    const unsigned long long t0 = clock64();
+    const float l_run = softmax_steps(lane_base, s_col, sm_iters);
+    const unsigned long long t1 = clock64();
+    if (lane == 0 && wi == 0) cycles[blockIdx.x * 3 + 1 + wg] = t1 - t0;
+    sink[blockIdx.x * blockDim.x + threadIdx.x] = l_run;
+  } else if (warp == 8 && lane == 0 && MMA_ON) {
+    const uint32_t q0 = base, k = base + 32768, v = base + 2 * 32768;
+    const uint32_t id_s = ptx::idesc_f16(128, 128, false, false);
+    const uint32_t id_pv = ptx::idesc_f16(128, 128, false, true);
+    const uint64_t qd = ptx::smem_desc_sw128(q0, 16, 1024);
+    const uint64_t kd = ptx::smem_desc_sw128(k, 16, 1024);
+    const uint64_t vd = ptx::smem_desc_sw128(v, 128 * 128, 1024);
+    const unsigned long long t0 = clock64();
+#pragma unroll 1
+    for (int it = 0; it < mma_iters; ++it) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        ptx::mma_ts(tmem + 128, tmem + kk * 8, vd + static_cast<uint64_t>(kk * 2048 >> 4), id_pv, 1u);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+        ptx::mma_ss(tmem, qd + off, kd + off, id_s, kk > 0 ? 1u : 0u);
+      }
+    }
+    ptx::mma_commit(ptx::smem_u32(&done));
+    bounded_wait(ptx::smem_u32(&done), 0);
+    cycles[blockIdx.x * 3] = clock64() - t0;
+  } else if (warp == 9 && lane == 0 && TMA_ON) {
+    // K tiles (128 x 128 f16, two 64-column boxes) of L2-resident heads into
+    // a ring; a slot is reloaded once its previous load has landed.
+    const uint32_t ring = base + 3 * 32768;
+    int t = 0;
+    for (; t < tma_tiles; ++t) {
+      const int slot = t % OVL_RING;
+      const uint32_t bar = ptx::smem_u32(&ring_full[slot]);
+      if (t >= OVL_RING && !bounded_wait(bar, ((t / OVL_RING) - 1) & 1)) break;
+      ptx::mbar_arrive_expect_tx(bar, TILE_BYTES);
+      const int tile = t % (4096 / BN), head = (blockIdx.x + t / (4096 / BN)) % heads;
+      for (int d = 0; d < D / 64; ++d)
+        ptx::tma_load_3d(ring + slot * TILE_BYTES + d * BN * 128, &tmK, bar, d * 64, tile * BN, head);
+    }
+    // every issued load lands before the CTA exits
+    for (int u = t > OVL_RING ? t - OVL_RING : 0; u < t; ++u)
+      if (!bounded_wait(ptx::smem_u32(&ring_full[u % OVL_RING]), (u / OVL_RING) & 1)) break;
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// issue: clock64 after each of kIssueN back-to-back MMAs of 128x128x16 (64
+// cycles of work each) issued by lane 0 of warp 8, SS form (A, B in shared
+// memory) or TS form (A in tensor memory), and at completion; CTA 0 reports.
+// With SOFTMAX, warps 0-7 run the softmax step on columns 256-511 meanwhile
+// (two of them share the issuer's sub-partition, as in the kernel) and the
+// issuer starts after ~4000 cycles, so they are in steady state.
+// ---------------------------------------------------------------------------
+constexpr int kIssueN = 24;
+
+template <bool TS, bool SOFTMAX>
+__global__ void __launch_bounds__(288, 1) issue_probe(unsigned long long* stamps, float* sink) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - ptx::smem_u32(smem_raw));
+  __shared__ uint32_t tmem_slot;
+  __shared__ __align__(8) uint64_t done;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 2 * 32768 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(g)[i] = 0;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(&done), 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_u32(&tmem_slot), 512);
+    ptx::tmem_relinquish();
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+  const uint32_t s_col = 256 + (warp / 4) * BN;
+  if (SOFTMAX && warp < 8) softmax_init(lane_base, s_col);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (SOFTMAX && warp < 8) {
+    sink[blockIdx.x * blockDim.x + threadIdx.x] = softmax_steps(lane_base, s_col, 6);
+  } else if (warp == 8 && lane == 0) {
+    if (SOFTMAX) {
+      const unsigned long long w0 = clock64();
+      while (clock64() - w0 < 4000) {
+      }
+    }
+    const uint32_t id_s = ptx::idesc_f16(128, 128, false, false);
+    const uint32_t id_pv = ptx::idesc_f16(128, 128, false, true);
+    const uint64_t qd = ptx::smem_desc_sw128(base, 16, 1024);
+    const uint64_t kd = ptx::smem_desc_sw128(base + 32768, 16, 1024);
+    const uint64_t vd = ptx::smem_desc_sw128(base + 32768, 128 * 128, 1024);
+    unsigned long long t[kIssueN + 2];
+    t[0] = clock64();
+#pragma unroll
+    for (int i = 0; i < kIssueN; ++i) {
+      if constexpr (TS)  // P V form: A (128 x 16) from tensor memory columns 0-63
+        ptx::mma_ts(tmem + 128, tmem + (i % 8) * 8,
+                    vd + static_cast<uint64_t>((i % 8) * 2048 >> 4), id_pv, 0u);
+      else
+        ptx::mma_ss(tmem + (i % 2) * 128, qd, kd, id_s, 0u);
+      t[i + 1] = clock64();
+    }
+    ptx::mma_commit(ptx::smem_u32(&done));
+    bounded_wait(ptx::smem_u32(&done), 0);
+    t[kIssueN + 1] = clock64();
+    if (blockIdx.x == 0)
+      for (int i = 0; i < kIssueN + 2; ++i) stamps[i] = t[i];
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+// issue rate: ISSUERS threads (lane 0 of warps 0 .. ISSUERS-1) each issue n
+// MMAs of 128 x 64 x 16 (32 cycles of work) into their own accumulators, in
+// a rolled loop.  If the cost of an issue is per thread, two issuers come
+// closer to the math rate; if it is per SM, they do not.
+template <int ISSUERS>
+__global__ void __launch_bounds__(128, 1) issue_rate_probe(int n, unsigned long long* cycles) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - ptx::smem_u32(smem_raw));
+  __shared__ uint32_t tmem_slot;
+  __shared__ __align__(8) uint64_t done[2];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 2 * 32768 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(g)[i] = 0;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(&done[0]), 1);
+    ptx::mbar_init(ptx::smem_u32(&done[1]), 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_u32(&tmem_slot), 512);
+    ptx::tmem_relinquish();
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  if (warp < ISSUERS && lane == 0) {
+    const uint32_t id = ptx::idesc_f16(128, 64, false, false);
+    const uint64_t qd = ptx::smem_desc_sw128(base, 16, 1024);
+    const uint64_t kd = ptx::smem_desc_sw128(base + 32768, 16, 1024);
+    const unsigned long long t0 = clock64();
+#pragma unroll 1
+    for (int i = 0; i < n; ++i) ptx::mma_ss(tmem + warp * 256 + (i & 1) * 64, qd, kd, id, 0u);
+    ptx::mma_commit(ptx::smem_u32(&done[warp]));
+    bounded_wait(ptx::smem_u32(&done[warp]), 0);
+    cycles[blockIdx.x * 2 + warp] = clock64() - t0;
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
 double mean_of(const std::vector<unsigned long long>& v, int stride, int off, int n) {
   double s = 0;
   int k = 0;
@@ -346,9 +635,9 @@ int main(int argc, char** argv) {
   cudaDeviceGetAttribute(&clk_khz, cudaDevAttrClockRate, 0);
   unsigned long long* cyc = nullptr;
   float* sink = nullptr;
-  cudaMalloc(&cyc, sizeof(unsigned long long) * 2 * sms);
-  cudaMalloc(&sink, sizeof(float) * 256 * sms);
-  std::vector<unsigned long long> h(2 * sms);
+  cudaMalloc(&cyc, sizeof(unsigned long long) * 3 * sms);
+  cudaMalloc(&sink, sizeof(float) * OVL_THREADS * sms);
+  std::vector<unsigned long long> h(3 * sms);
   int rc = 0;
 
   if (all || !std::strcmp(which, "tma")) {
@@ -414,6 +703,83 @@ int main(int argc, char** argv) {
     std::printf("softmax  128 x %d tile, two warpgroups per SM:  %6.0f / %6.0f cycles / tile "
                 "(MUFU floor %d per warpgroup alone)\n",
                 BN, mean_of(h, 2, 0, sms) / iters, mean_of(h, 2, 1, sms) / iters, BN * 8);
+  }
+  if (all || !std::strcmp(which, "overlap")) {
+    const int heads = 16, S = 4096;
+    void* K = nullptr;
+    const size_t bytes = static_cast<size_t>(heads) * S * D * 2;
+    cudaMalloc(&K, bytes);
+    cudaMemset(K, 0, bytes);
+    CUtensorMap mk;
+    if (!make_map(&mk, K, heads, S)) {
+      std::printf("overlap: tensor map encoding failed\n");
+      return 1;
+    }
+    // MMA iterations (1024 tensor cycles each) and K tiles sized to span the
+    // softmax run (~2250 cycles per tile and warpgroup pair).
+    const int mma_iters = 256, sm_iters = 112, tma_tiles = 640;
+    auto launch = [&](auto kern, double& mma_c, double& sm_c) -> bool {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, OVL_SMEM);
+      cudaMemset(cyc, 0, sizeof(unsigned long long) * 3 * sms);
+      for (int rep = 0; rep < 2; ++rep)
+        kern<<<sms, OVL_THREADS, OVL_SMEM>>>(mk, heads, tma_tiles, mma_iters, sm_iters, cyc, sink);
+      if (!check("overlap")) return false;
+      cudaMemcpy(h.data(), cyc, sizeof(unsigned long long) * 3 * sms, cudaMemcpyDeviceToHost);
+      // 3 stamps per CTA: MMA, softmax warpgroup 0, softmax warpgroup 1
+      mma_c = mean_of(h, 3, 0, sms) / mma_iters;
+      sm_c = 0.5 * (mean_of(h, 3, 1, sms) + mean_of(h, 3, 2, sms)) / sm_iters;
+      return true;
+    };
+    double m[4], x[4], unused;
+    if (!launch(overlap_probe<true, false, false>, m[0], unused)) return 1;
+    if (!launch(overlap_probe<false, true, false>, unused, x[0])) return 1;
+    if (!launch(overlap_probe<true, true, false>, m[1], x[1])) return 1;
+    if (!launch(overlap_probe<true, false, true>, m[2], unused)) return 1;
+    if (!launch(overlap_probe<true, true, true>, m[3], x[3])) return 1;
+    std::printf("overlap  one tile's P V + S (1024 tensor cycles), cycles / iteration: alone %.0f, "
+                "with two softmax warpgroups %.0f, with a TMA K stream %.0f, with both %.0f\n",
+                m[0], m[1], m[2], m[3]);
+    std::printf("overlap  softmax 128 x %d, two warpgroups, cycles / tile: alone %.0f, with the MMAs "
+                "%.0f, with the MMAs and the TMA stream %.0f\n", BN, x[0], x[1], x[3]);
+    cudaFree(K);
+  }
+
+  if (all || !std::strcmp(which, "issue")) {
+    unsigned long long* st = nullptr;
+    cudaMalloc(&st, sizeof(unsigned long long) * (kIssueN + 2));
+    for (int v = 0; v < 4; ++v) {
+      const bool ts = v & 1, sm = v & 2;
+      auto kern = sm ? (ts ? issue_probe<true, true> : issue_probe<false, true>)
+                     : (ts ? issue_probe<true, false> : issue_probe<false, false>);
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_SMEM);
+      cudaMemset(st, 0, sizeof(unsigned long long) * (kIssueN + 2));
+      for (int rep = 0; rep < 2; ++rep) kern<<<sms, 288, MMA_SMEM>>>(st, sink);
+      if (!check("issue")) return 1;
+      std::vector<unsigned long long> hs(kIssueN + 2);
+      cudaMemcpy(hs.data(), st, sizeof(unsigned long long) * (kIssueN + 2), cudaMemcpyDeviceToHost);
+      std::printf("issue    %d MMAs of 128x128x16 (%s, 64 cycles each) by one thread%s: return of "
+                  "issue i (cycles after the first issue):", kIssueN,
+                  ts ? "A from tensor memory" : "A, B from shared memory",
+                  sm ? " beside two softmax warpgroups" : "");
+      for (int i = 0; i < kIssueN; ++i) std::printf(" %llu", hs[i + 1] - hs[0]);
+      std::printf("; all complete at %llu\n", hs[kIssueN + 1] - hs[0]);
+    }
+    cudaFree(st);
+
+    const int total = 512;  // MMAs of 128 x 64 x 16 per CTA, 32 cycles of work each
+    double c[2];
+    for (int k = 0; k < 2; ++k) {
+      auto kern = k == 0 ? issue_rate_probe<1> : issue_rate_probe<2>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_SMEM);
+      cudaMemset(cyc, 0, sizeof(unsigned long long) * 3 * sms);
+      for (int rep = 0; rep < 2; ++rep) kern<<<sms, 128, MMA_SMEM>>>(total / (k + 1), cyc);
+      if (!check("issue")) return 1;
+      cudaMemcpy(h.data(), cyc, sizeof(unsigned long long) * 2 * sms, cudaMemcpyDeviceToHost);
+      c[k] = k == 0 ? mean_of(h, 2, 0, sms) : std::max(mean_of(h, 2, 0, sms), mean_of(h, 2, 1, sms));
+    }
+    std::printf("issue    %d MMAs of 128x64x16 (32 cycles of work each, rolled loop): one issuing "
+                "thread %.1f cycles / MMA, two issuing threads %.1f\n", total, c[0] / total,
+                c[1] / total);
   }
   cudaFree(cyc);
   cudaFree(sink);
