@@ -191,6 +191,13 @@ constexpr int kPolyPairsOf8 = ATTNPROF_POLY_PAIRS_OF_8;
 #endif
 constexpr int kPsplitQuarters = ATTNPROF_PSPLIT_QUARTERS;
 
+// 1 (default): with one S buffer per Q tile, no per-step O_DONE commit (see
+// AttnConfig::ODONE_PER_STEP); 0 commits it every step as two-buffer tiles do.
+#ifndef ATTNPROF_LEAN_COMMITS
+#define ATTNPROF_LEAN_COMMITS 1
+#endif
+constexpr bool kLeanCommits = ATTNPROF_LEAN_COMMITS != 0;
+
 
 // PAIR: the CTA is one of a cluster pair that shares every K/V tile through
 // cta_group::2 MMAs of M = 256 (tile i of the even CTA on rows 0-127, tile i
@@ -266,6 +273,15 @@ struct AttnConfig {
       (BN / 32) * PSPLIT_QUARTERS / 4 >= 1 ? (BN / 32) * PSPLIT_QUARTERS / 4 : 1;
   static constexpr int BAR_P_READY = BAR_S_FULL + NQ * NSBUF;      // [NQ][NSBUF][PHALVES]
   static constexpr int BAR_O_DONE = BAR_P_READY + NQ * NSBUF * PHALVES;  // every P V of tile i
+  // Is O_DONE committed after every step?  With one S buffer per tile,
+  // S_i(j+1) is issued behind P_i(j) V_j by the same thread, and a commit
+  // covers every earlier MMA of its thread: the S_FULL that the softmax
+  // waits for before step j+1 already says that P_i(j) V_j is complete, so a
+  // rescale of O needs no O_DONE, and the commit (~50-120 cycles of the
+  // issuing thread, which is short of slack) is left out.  Two S buffers
+  // issue S_i(j+1) one step earlier, so they keep it.  Profiled builds keep
+  // it too, for the observer that stamps each P V's completion.
+  static constexpr bool ODONE_PER_STEP = NSBUF == 2 || !kLeanCommits;
   static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
   static constexpr int BAR_DRAIN = BAR_O_FINAL + NQ;
   static constexpr int NUM_BARS = BAR_DRAIN + 1;
@@ -596,13 +612,13 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
       if (!ok) break;
       // The tile's next S follows its last P V MMAs directly; the O commits
       // come after it (O_DONE then also covers that S, which every waiter on
-      // O_DONE has already seen complete).
+      // O_DONE has already seen complete).  S_FULL covers this step's P V.
       if (jn < n) {
         if (i == 0) prof.stamp(kPhQK, jn, 0);
         issue_s(i, jn, sk);
         signal(bar(C::BAR_S_FULL + i * C::NSBUF + jn % C::NSBUF));
       }
-      signal(bar(C::BAR_O_DONE + i));
+      if (C::ODONE_PER_STEP || PROFILE) signal(bar(C::BAR_O_DONE + i));
       if (j == n - 1) signal(bar(C::BAR_O_FINAL + i));
       prof.stamp(kPhMmaT0 + i, j, 1);
     }
@@ -759,11 +775,14 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       resc = true;
     }
     if (__any_sync(0xffffffffu, resc)) {
-      // O holds the sum through PV(j-1); wait for that MMA, then scale in place.
-      ok = __all_sync(0xffffffffu,
-                      wait_bar(bar(C::BAR_O_DONE + qi), (j - 1) & 1, w, kSiteODone));
-      if (!ok) break;
-      ptx::tc_fence_after();
+      // O holds the sum through PV(j-1); wait for that MMA, then scale in
+      // place.  With one S buffer the S_FULL observed above already covers it.
+      if constexpr (C::ODONE_PER_STEP) {
+        ok = __all_sync(0xffffffffu,
+                        wait_bar(bar(C::BAR_O_DONE + qi), (j - 1) & 1, w, kSiteODone));
+        if (!ok) break;
+        ptx::tc_fence_after();
+      }
 #pragma unroll 1
       for (int c = 0; c < C::D / 32; ++c) {
         uint32_t o[32];

@@ -490,17 +490,20 @@ __global__ void __launch_bounds__(OVL_THREADS, 1)
 // ---------------------------------------------------------------------------
 constexpr int kIssueN = 24;
 
-template <bool TS, bool SOFTMAX>
+template <bool TS, bool SOFTMAX, bool COMMITS = false>
 __global__ void __launch_bounds__(288, 1) issue_probe(unsigned long long* stamps, float* sink) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - ptx::smem_u32(smem_raw));
   __shared__ uint32_t tmem_slot;
-  __shared__ __align__(8) uint64_t done;
+  __shared__ __align__(8) uint64_t done, group_done;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < 2 * 32768 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(g)[i] = 0;
   if (threadIdx.x == 0) {
     ptx::mbar_init(ptx::smem_u32(&done), 1);
+    // one arrival per commit; nothing waits on it (the probe only times the
+    // issues around each commit)
+    ptx::mbar_init(ptx::smem_u32(&group_done), 1);
     ptx::fence_mbar_init();
   }
   if (warp == 0) {
@@ -540,6 +543,7 @@ __global__ void __launch_bounds__(288, 1) issue_probe(unsigned long long* stamps
                     vd + static_cast<uint64_t>((i % 8) * 2048 >> 4), id_pv, 0u);
       else
         ptx::mma_ss(tmem + (i % 2) * 128, qd, kd, id_s, 0u);
+      if (COMMITS && i % 8 == 7 && i + 1 < kIssueN) ptx::mma_commit(ptx::smem_u32(&group_done));
       t[i + 1] = clock64();
     }
     ptx::mma_commit(ptx::smem_u32(&done));
@@ -747,9 +751,10 @@ int main(int argc, char** argv) {
   if (all || !std::strcmp(which, "issue")) {
     unsigned long long* st = nullptr;
     cudaMalloc(&st, sizeof(unsigned long long) * (kIssueN + 2));
-    for (int v = 0; v < 4; ++v) {
-      const bool ts = v & 1, sm = v & 2;
-      auto kern = sm ? (ts ? issue_probe<true, true> : issue_probe<false, true>)
+    for (int v = 0; v < 5; ++v) {
+      const bool ts = v & 1, sm = v & 2, cm = v == 4;
+      auto kern = cm ? issue_probe<false, false, true>
+                : sm ? (ts ? issue_probe<true, true> : issue_probe<false, true>)
                      : (ts ? issue_probe<true, false> : issue_probe<false, false>);
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_SMEM);
       cudaMemset(st, 0, sizeof(unsigned long long) * (kIssueN + 2));
@@ -760,7 +765,7 @@ int main(int argc, char** argv) {
       std::printf("issue    %d MMAs of 128x128x16 (%s, 64 cycles each) by one thread%s: return of "
                   "issue i (cycles after the first issue):", kIssueN,
                   ts ? "A from tensor memory" : "A, B from shared memory",
-                  sm ? " beside two softmax warpgroups" : "");
+                  cm ? ", a commit after every 8th" : sm ? " beside two softmax warpgroups" : "");
       for (int i = 0; i < kIssueN; ++i) std::printf(" %llu", hs[i + 1] - hs[0]);
       std::printf("; all complete at %llu\n", hs[kIssueN + 1] - hs[0]);
     }
