@@ -282,6 +282,17 @@ struct AttnConfig {
   // issue S_i(j+1) one step earlier, so they keep it.  Profiled builds keep
   // it too, for the observer that stamps each P V's completion.
   static constexpr bool ODONE_PER_STEP = NSBUF == 2 || !kLeanCommits;
+  // Ring releases.  With one S buffer the ring items are K_0, then V_j,
+  // K_{j+1} for each step j, and V_j and K_{j+1} are both free once step j's
+  // MMAs (P V_j of every tile, then S(j+1)) complete, so one commit, on
+  // K_{j+1}'s EMPTY barrier, releases both, and V slots get none.  K_m is
+  // item 2m, in slot 2m mod STAGES; the K items that share a slot recur every
+  // K_SLOT_PERIOD of them, so K_m's commit completes phase m / K_SLOT_PERIOD
+  // of that barrier.  The producer reloading slot t mod STAGES (item t >=
+  // STAGES) waits for the commit of K_m with m = (t - STAGES + 1) / 2: the
+  // previous occupant of the slot is K_m itself or V_{m-1}.
+  static constexpr bool V_RELEASE_WITH_K = kLeanCommits && NSBUF == 1;
+  static constexpr int K_SLOT_PERIOD = STAGES % 2 == 0 ? STAGES / 2 : STAGES;
   static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
   static constexpr int BAR_DRAIN = BAR_O_FINAL + NQ;
   static constexpr int NUM_BARS = BAR_DRAIN + 1;
@@ -446,10 +457,20 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
 
   auto produce = [&](bool is_k, int j) {
     const int s = t % C::STAGES;
-    const int r = t / C::STAGES;
-    if (r > 0 && !wait_bar(bar(C::BAR_KV_EMPTY + s), (r - 1) & 1, w, kSiteKvEmpty)) {
-      ok = false;
-      return;
+    if (t >= C::STAGES) {
+      uint32_t eb, par;
+      if constexpr (C::V_RELEASE_WITH_K) {
+        const int m = (t - C::STAGES + 1) / 2;  // the K item whose commit frees slot s
+        eb = bar(C::BAR_KV_EMPTY + (2 * m) % C::STAGES);
+        par = static_cast<uint32_t>(m / C::K_SLOT_PERIOD) & 1u;
+      } else {
+        eb = bar(C::BAR_KV_EMPTY + s);
+        par = static_cast<uint32_t>(t / C::STAGES - 1) & 1u;
+      }
+      if (!wait_bar(eb, par, w, kSiteKvEmpty)) {
+        ok = false;
+        return;
+      }
     }
     prof.stamp(is_k ? kPhLoadK : kPhLoadV, j, 0);
     ptx::mbar_arrive_expect_tx(bar(C::BAR_KV_FULL + s), C::KV_TILE_BYTES);
@@ -623,8 +644,8 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
       prof.stamp(kPhMmaT0 + i, j, 1);
     }
     if (!ok) break;
-    signal(bar(C::BAR_KV_EMPTY + sv));
-    if (sk >= 0) signal(bar(C::BAR_KV_EMPTY + sk));
+    if constexpr (!C::V_RELEASE_WITH_K) signal(bar(C::BAR_KV_EMPTY + sv));
+    if (sk >= 0) signal(bar(C::BAR_KV_EMPTY + sk));  // with V_RELEASE_WITH_K: V_j's slot too
   }
 
   // Drain: every MMA this thread issued has completed before TMEM is freed.
