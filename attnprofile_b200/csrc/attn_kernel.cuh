@@ -562,20 +562,21 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
     qd0[i] = ptx::smem_desc_sw128(sbase + C::OFF_Q + i * C::Q_TILE_BYTES, 16, 1024);
   const uint64_t kd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, 16, 1024);
   const uint64_t vd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, C::V_BLK_BYTES, 1024);
-  auto slot_off = [](int stage) -> uint64_t {
-    return static_cast<uint64_t>((stage * C::KV_TILE_BYTES) >> 4);
+  auto slot_off = [](int stage) -> uint32_t {
+    return static_cast<uint32_t>((stage * C::KV_TILE_BYTES) >> 4);
   };
 
   // S_i(j) = Q_i K_j^T : D/16 MMAs of 128 x BN x 16.  K-step kk reads 16
   // elements (32 B) of every 128 B row of 64-column block kk / 4.
   auto issue_s = [&](int i, int j, int stage) {
     const uint32_t d_tmem = tmem + (i * C::NSBUF + j % C::NSBUF) * C::BN;
-    const uint64_t kd = kd0 + slot_off(stage);
+    const uint64_t kd = ptx::desc_add(kd0, slot_off(stage));
 #pragma unroll
     for (int kk = 0; kk < KSTEPS_S; ++kk) {
-      const uint64_t qo = static_cast<uint64_t>(((kk >> 2) * C::Q_BLK_BYTES + (kk & 3) * 32) >> 4);
-      const uint64_t ko = static_cast<uint64_t>(((kk >> 2) * C::K_BLK_BYTES + (kk & 3) * 32) >> 4);
-      ptx::mma_ss<G>(d_tmem, qd0[i] + qo, kd + ko, C::IDESC_S, kk > 0 ? 1u : 0u);
+      const uint32_t qo = static_cast<uint32_t>(((kk >> 2) * C::Q_BLK_BYTES + (kk & 3) * 32) >> 4);
+      const uint32_t ko = static_cast<uint32_t>(((kk >> 2) * C::K_BLK_BYTES + (kk & 3) * 32) >> 4);
+      ptx::mma_ss<G>(d_tmem, ptx::desc_add(qd0[i], qo), ptx::desc_add(kd, ko), C::IDESC_S,
+                     kk > 0 ? 1u : 0u);
     }
   };
   // O_i += P_i(j) V_j : BN/16 MMAs of 128 x D x 16, A = P from TMEM; K-step
@@ -583,11 +584,11 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
   auto issue_pv = [&](int i, int j, int stage, int k0, int k1) {
     const uint32_t p_tmem = tmem + (i * C::NSBUF + j % C::NSBUF) * C::BN;
     const uint32_t o_tmem = tmem + C::TMEM_O_COL + i * C::D;
-    const uint64_t vd = vd0 + slot_off(stage);
+    const uint64_t vd = ptx::desc_add(vd0, slot_off(stage));
 #pragma unroll
     for (int kk = k0; kk < k1; ++kk)
-      ptx::mma_ts<G>(o_tmem, p_tmem + kk * 8, vd + static_cast<uint64_t>(kk * 2048 >> 4),
-                  C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+      ptx::mma_ts<G>(o_tmem, p_tmem + kk * 8, ptx::desc_add(vd, static_cast<uint32_t>(kk * 2048 >> 4)),
+                     C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
   };
 
   // Prologue: S for the first NSBUF KV tiles.

@@ -371,6 +371,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// A descriptor advanced by `off16` (a byte offset >> 4) in its start-address
+// field, with a 32-bit add on the low word: callers guarantee that the field
+// (bits 0-13) does not carry, so the high word is unchanged.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t off16) {
+  const uint32_t lo = static_cast<uint32_t>(d) + off16;
+  const uint32_t hi = static_cast<uint32_t>(d >> 32);
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+
 // Instruction descriptor for kind::f16 with f32 accumulation.
 //   [4,6) D format (1 = f32)  [7,10) A format  [10,13) B format (0 f16, 1 bf16)
 //   [15] A major (0 = K)  [16] B major (0 = K, 1 = MN)  [17,23) N >> 3  [24,29) M >> 4
