@@ -7,7 +7,8 @@
 //
 //   * one TMA producer warp loads the Q tile(s) once and streams K and V tiles
 //     through a STAGES-deep ring of 128B-swizzled shared-memory slots guarded
-//     by full/empty mbarrier pairs;
+//     by full/empty mbarriers (with one S buffer per tile, one empty commit
+//     per step frees both the V_j and the K_{j+1} slot);
 //   * one MMA warp (a single elected lane; one per Q tile when S is
 //     double-buffered in a two-tile CTA) issues tcgen05.mma:
 //       S_i = Q_i K_j^T    (A, B from shared memory, D in TMEM, f32)
