@@ -198,6 +198,11 @@ constexpr int kPsplitQuarters = ATTNPROF_PSPLIT_QUARTERS;
 #define ATTNPROF_LEAN_COMMITS 1
 #endif
 constexpr bool kLeanCommits = ATTNPROF_LEAN_COMMITS != 0;
+// 1 (default): one FULL wait per step for V_j and K_{j+1} (AttnConfig::KV_JOINT_FULL).
+#ifndef ATTNPROF_JOINT_FULL
+#define ATTNPROF_JOINT_FULL 1
+#endif
+constexpr bool kJointFull = ATTNPROF_JOINT_FULL != 0;
 
 
 // PAIR: the CTA is one of a cluster pair that shares every K/V tile through
@@ -293,6 +298,13 @@ struct AttnConfig {
   // STAGES) waits for the commit of K_m with m = (t - STAGES + 1) / 2: the
   // previous occupant of the slot is K_m itself or V_{m-1}.
   static constexpr bool V_RELEASE_WITH_K = kLeanCommits && NSBUF == 1;
+  // Joint landing (single CTAs): V_j and K_{j+1} complete on V_j's FULL
+  // barrier (armed for both tiles' bytes), so the MMA issuer makes one wait
+  // per step instead of two -- its waits cost it ~100 cycles each and it is
+  // on the per-tile chain.  K_{j+1}'s own FULL barrier still gets one plain
+  // arrival from the producer, so every slot's barrier advances one phase per
+  // item and the phase parities stay (t / STAGES) & 1.
+  static constexpr bool KV_JOINT_FULL = kJointFull && V_RELEASE_WITH_K && !PAIR;
   static constexpr int K_SLOT_PERIOD = STAGES % 2 == 0 ? STAGES / 2 : STAGES;
   static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
   static constexpr int BAR_DRAIN = BAR_O_FINAL + NQ;
@@ -456,7 +468,9 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
   for (int s = 0; s < C::STAGES; ++s) last_issued[s] = -1;
   bool ok = true;
 
-  auto produce = [&](bool is_k, int j) {
+  // joint: this V item's FULL barrier also takes the next K item's bytes
+  // (KV_JOINT_FULL); k_bar: the barrier a K item's load completes on (-1: its own).
+  auto produce = [&](bool is_k, int j, bool joint = false, int k_bar = -1) {
     const int s = t % C::STAGES;
     if (t >= C::STAGES) {
       uint32_t eb, par;
@@ -474,20 +488,26 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
       }
     }
     prof.stamp(is_k ? kPhLoadK : kPhLoadV, j, 0);
-    ptx::mbar_arrive_expect_tx(bar(C::BAR_KV_FULL + s), C::KV_TILE_BYTES);
+    uint32_t full = bar(C::BAR_KV_FULL + s);
+    if (k_bar >= 0) {
+      ptx::mbar_arrive(full);  // keeps this slot's phase count; the bytes go to k_bar
+      full = bar(C::BAR_KV_FULL + k_bar);
+    } else {
+      ptx::mbar_arrive_expect_tx(full, joint ? 2 * C::KV_TILE_BYTES : C::KV_TILE_BYTES);
+    }
     const uint32_t dst = sbase + C::OFF_KV + s * C::KV_TILE_BYTES;
     const int key0 = (wt.kv_lo + j) * C::BN;
     if (is_k) {
       // K: keys [key0 + rank * K_ROWS, + K_ROWS), all D columns.
 #pragma unroll
       for (int d = 0; d < C::DBLK; ++d)
-        ptx::tma_load_3d_hint(dst + d * C::K_BLK_BYTES, tmK, bar(C::BAR_KV_FULL + s), d * 64,
+        ptx::tma_load_3d_hint(dst + d * C::K_BLK_BYTES, tmK, full, d * 64,
                               key0 + wt.rank * C::K_ROWS, bh, pol_kv);
     } else {
       // V: all BN keys, column blocks [rank * V_DBLK, + V_DBLK).
 #pragma unroll
       for (int d = 0; d < C::V_DBLK; ++d)
-        ptx::tma_load_3d_hint(dst + d * C::V_BLK_BYTES, tmV, bar(C::BAR_KV_FULL + s),
+        ptx::tma_load_3d_hint(dst + d * C::V_BLK_BYTES, tmV, full,
                               (wt.rank * C::V_DBLK + d) * 64, key0, bh, pol_kv);
     }
     last_issued[s] = t;
@@ -496,8 +516,10 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
 
   for (int jj = 0; jj < C::NSBUF && jj < n && ok; ++jj) produce(true, jj);
   for (int j = 0; j < n && ok; ++j) {
-    produce(false, j);
-    if (ok && j + C::NSBUF < n) produce(true, j + C::NSBUF);
+    const bool joint = C::KV_JOINT_FULL && j + C::NSBUF < n;
+    const int sv = t % C::STAGES;
+    produce(false, j, joint);
+    if (ok && j + C::NSBUF < n) produce(true, j + C::NSBUF, false, joint ? sv : -1);
   }
   if (!ok) {
     // Do not leave this CTA with bulk copies in flight: wait (bounded) for the
@@ -609,6 +631,8 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
     if (i0 == 0) prof.stamp(kPhVWait, j, 0);
     if (!(ok = ring_wait(sv, false, j))) break;
     if (i0 == 0) prof.stamp(kPhVWait, j, 1);
+    // K_{j+1} landed with V_j: its load ends here for the profiler.
+    if (C::KV_JOINT_FULL && i0 == 0 && j + 1 < n) prof.stamp(kPhLoadK, j + 1, 1);
     const int jn = j + C::NSBUF;
     int sk = -1;
     for (int i = i0; i < i1 && ok; ++i) {
@@ -619,9 +643,14 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
         // K_{j+NSBUF} is normally resident long before the last P part: its
         // wait sits here, off the path from that P part to the next S.
         if (h == C::PHALVES - 1 && jn < n && sk < 0) {
-          if (i0 == 0) prof.stamp(kPhKWait, j, 0);
-          if (!(ok = ring_wait(sk, true, jn))) break;
-          if (i0 == 0) prof.stamp(kPhKWait, j, 1);
+          if constexpr (C::KV_JOINT_FULL) {
+            sk = t % C::STAGES;  // landed with V_j (waited for above)
+            ++t;
+          } else {
+            if (i0 == 0) prof.stamp(kPhKWait, j, 0);
+            if (!(ok = ring_wait(sk, true, jn))) break;
+            if (i0 == 0) prof.stamp(kPhKWait, j, 1);
+          }
         }
         if (!(ok = wait_bar(bar(pb + h), (j / C::NSBUF) & 1, w, kSitePReady))) break;
         ptx::tc_fence_after();
