@@ -285,8 +285,8 @@ struct AttnConfig {
   // waits for before step j+1 already says that P_i(j) V_j is complete, so a
   // rescale of O needs no O_DONE, and the commit (~50-120 cycles of the
   // issuing thread, which is short of slack) is left out.  Two S buffers
-  // issue S_i(j+1) one step earlier, so they keep it.  Profiled builds keep
-  // it too, for the observer that stamps each P V's completion.
+  // issue S_i(j+1) one step earlier, so they keep it.  (The profiler's
+  // observer then reads each P V's completion from that S_FULL.)
   static constexpr bool ODONE_PER_STEP = NSBUF == 2 || !kLeanCommits;
   // Ring releases.  With one S buffer the ring items are K_0, then V_j,
   // K_{j+1} for each step j, and V_j and K_{j+1} are both free once step j's
@@ -670,7 +670,7 @@ __device__ void mma_role(uint32_t tmem, uint32_t sbase, const WorkTile& wt, cons
         issue_s(i, jn, sk);
         signal(bar(C::BAR_S_FULL + i * C::NSBUF + jn % C::NSBUF));
       }
-      if (C::ODONE_PER_STEP || PROFILE) signal(bar(C::BAR_O_DONE + i));
+      if (C::ODONE_PER_STEP) signal(bar(C::BAR_O_DONE + i));
       if (j == n - 1) signal(bar(C::BAR_O_FINAL + i));
       prof.stamp(kPhMmaT0 + i, j, 1);
     }
@@ -1113,13 +1113,38 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
 // Profiler observer: stamps the completion of each P V of Q tile 0.  It only
 // watches; a missed phase costs a stamp, never an error status.  It waits
 // with a suspend hint so it does not take issue slots from the softmax warps
-// of its SM sub-partition (a polling observer slowed them visibly).
+// of its SM sub-partition (a polling observer slowed them visibly).  Where
+// O_DONE is not committed every step (one S buffer), the completion of
+// P_0(j) V_j is that of S_0(j+1), committed right behind it by the same
+// thread, and the last step's is O_FINAL; the profiled kernel thus commits
+// exactly what the production kernel does.
 template <class C>
 __device__ void observer_role(uint32_t sbase, int n, const WaitCtx& w, const Prof<true>& prof) {
-  const uint32_t bar = sbase + C::OFF_BAR + 8u * (C::BAR_O_DONE + 0);
-  for (int j = 0; j < n; ++j) {
+  if (!C::ODONE_PER_STEP && n > 1) {
+    // Step past S_0(0), the first completion of S_FULL (a parity-1 wait on a
+    // fresh barrier would return at once), so that the k-th wait below is
+    // for the (k+1)-th completion.
+    const uint32_t bar = sbase + C::OFF_BAR + 8u * (C::BAR_S_FULL + 0);
     const unsigned long long t0 = ptx::globaltimer_ns();
-    while (!ptx::mbar_try_wait_sleep(bar, j & 1, 100000u)) {
+    while (!ptx::mbar_try_wait_sleep(bar, 0, 100000u)) {
+      if (*w.abort || ptx::globaltimer_ns() - t0 > w.timeout_ns) return;
+    }
+  }
+  for (int j = 0; j < n; ++j) {
+    uint32_t b, parity;
+    if (C::ODONE_PER_STEP) {
+      b = C::BAR_O_DONE + 0;
+      parity = j & 1;
+    } else if (j + 1 < n) {
+      b = C::BAR_S_FULL + 0;  // tile 0, the only S buffer
+      parity = (j + 1) & 1;
+    } else {
+      b = C::BAR_O_FINAL + 0;
+      parity = 0;
+    }
+    const uint32_t bar = sbase + C::OFF_BAR + 8u * b;
+    const unsigned long long t0 = ptx::globaltimer_ns();
+    while (!ptx::mbar_try_wait_sleep(bar, parity, 100000u)) {
       if (*w.abort || ptx::globaltimer_ns() - t0 > w.timeout_ns) return;
     }
     prof.stamp(kPhPV, j, 1);
