@@ -7,7 +7,9 @@ of the profiler-enabled kernel variant (attn_fwd_profiled) writes clock64
 begin/end stamps per KV iteration (first 32 iterations, one slot each):
 
   LoadQ    producer issues the Q TMA            -> MMA warp sees Q landed
-  LoadK    producer issues K_j (slot free)      -> MMA warp sees K_j landed
+  LoadK    producer issues K_j (slot free)      -> MMA warp sees K_j landed (in
+           single one-buffer CTAs K_j lands with V_{j-1}, on one barrier, so
+           this is the V_{j-1} wait and the K-wait trace phase stays empty)
   LoadV    producer issues V_j (slot free)      -> MMA warp sees V_j landed
   GEMM-QK  MMA warp issues S_0 = Q_0 K_j^T       -> softmax warp sees S_0 complete
   SOFTMAX  softmax warp sees S_0                 -> P_0 written to TMEM and signalled
