@@ -201,7 +201,8 @@ def test_repeat_calls_are_deterministic(engine):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("BM,BN", [(256, 128), (128, 128), (128, 256), (128, 64), (256, 32)])
+@pytest.mark.parametrize("BM,BN", [(256, 128), (128, 128), (128, 256), (128, 64), (256, 32), (256, 96),
+                                   (512, 128)])
 @pytest.mark.parametrize("ramp", ["up", "down"])
 def test_parity_moving_row_max(engine, oracle_mod, BM, BN, ramp):
     """Keys scaled by a ramp over the sequence.  'up' makes the row max grow by
