@@ -72,6 +72,7 @@ struct LaunchOpts {
   int split = 0;                 // 0: automatic, 1: never split, k >= 2: split k ways
   void* workspace = nullptr;     // caller-provided workspace (else stream-ordered pool)
   size_t workspace_bytes = 0;
+  bool no_pool = false;          // never fall back to the pool: a split plan needs `workspace`
   SplitPlan* plan_out = nullptr; // receives the plan
   bool plan_only = false;        // compute the plan, launch nothing
   bool cache_maps = true;        // false: encode tensor maps per call, no host allocation
@@ -343,6 +344,8 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   uint8_t* ws = nullptr;
   bool pooled = false;
   if (plan.split > 1) {
+    if (o.no_pool && (o.workspace == nullptr || o.workspace_bytes < plan.ws_bytes))
+      return ATTN_ERR_SCRATCH_LIMIT;
     if (o.workspace != nullptr) {
       if (o.workspace_bytes < plan.ws_bytes) return ATTN_ERR_RESOURCE;
       ws = static_cast<uint8_t*>(o.workspace);

@@ -523,7 +523,12 @@ __device__ void load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const 
   }
   if (!ok) {
     // Do not leave this CTA with bulk copies in flight: wait (bounded) for the
-    // most recent load issued into every slot to land.
+    // most recent load issued into every slot to land.  Under the joint
+    // landing a K item's bytes complete V_j's barrier (slot sv), not its own,
+    // whose phase the plain arrival completed at once; that K load was issued
+    // right after V_j into sv's phase, so the wait on slot sv below covers it
+    // (slot sv cannot have been reloaded since: a reload first waits for the
+    // commit that releases both V_j and K_{j+1}).
 #pragma unroll
     for (int s = 0; s < C::STAGES; ++s) {
       if (last_issued[s] < 0) continue;

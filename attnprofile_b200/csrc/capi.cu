@@ -94,20 +94,26 @@ static int dispatch(const void* Q, const void* K, const void* V, void* O, int B,
             : dispatch_attn<__nv_bfloat16, 128, false>(BM, BN, Q, K, V, O, B, H, S, SQO, SKV, st, o);
 }
 
+// The key-split mode attn_set_split last stored.
+int current_split_mode() { return g_split_mode.load(); }
+
 // Launch with a caller-provided workspace and per-call tensor maps (no
-// device or host allocation); the other settings as for attn_fwd.  When
-// plan_only is set, only *plan is filled.  Used by attn_fwd_noalloc.
+// device or host allocation, never the stream-ordered pool: a plan that
+// needs more than ws_bytes returns ATTN_ERR_SCRATCH_LIMIT); split_mode as
+// for attn_set_split, the other settings as for attn_fwd.  When plan_only is
+// set, only *plan is filled.  Used by attn_fwd_noalloc.
 int run_in_workspace(const void* Q, const void* K, const void* V, void* O, int B, int H, int S,
-                     int D, int dtype, int BM, int BN, cudaStream_t st, void* ws,
+                     int D, int dtype, int BM, int BN, cudaStream_t st, int split_mode, void* ws,
                      size_t ws_bytes, SplitPlan* plan, bool plan_only) {
   const int v = validate(Q, K, V, O, B, H, S, D, S, S, dtype);
   if (v <= 0) return v;
   LaunchOpts o;
   o.timeout_ns = g_timeout_ns.load();
   o.fault_mode = g_fault_mode.load();
-  o.split = g_split_mode.load();
+  o.split = split_mode;
   o.workspace = ws;
   o.workspace_bytes = ws_bytes;
+  o.no_pool = true;
   o.plan_out = plan;
   o.plan_only = plan_only;
   o.cache_maps = false;

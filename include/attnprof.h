@@ -161,22 +161,32 @@ int attn_query_split(int B, int H, int S, int D, int dtype, int BM, int BN, int*
 
 /*
  * attn_fwd_noalloc -- attn_fwd for callers that must not allocate GPU
- * memory: code running inside a CUDA graph being captured, a host thread that
- * holds a preallocated memory budget, or an allocator callback.  Arguments
- * and results are those of attn_fwd.  When the launch's plan splits units
- * along the keys (attn_set_split / attn_query_split) it needs scratch for the
- * partial results; attn_fwd takes that from a stream-ordered pool, this entry
- * point from a fixed array of ATTN_NOALLOC_SCRATCH_BYTES that the library
- * holds in every GPU's memory from the first call on that GPU until the
- * process exits.  It calls no cudaMalloc / cudaFree / pool allocation, and
- * encodes its tensor maps per call instead of caching them.
+ * memory when they launch: a serving process that reserved its whole memory
+ * budget at start-up and hands its kernels pre-sized buffers, a custom
+ * allocator (or code it calls back) that must not re-enter the CUDA
+ * allocator, a latency-bound loop that cannot take the device-wide stall of
+ * cudaMalloc / cudaFree.  Arguments and results are those of attn_fwd.  When
+ * the launch's plan splits units along the keys (attn_set_split /
+ * attn_query_split) it needs scratch for the partial results; attn_fwd takes
+ * that from a stream-ordered pool, this entry point from a fixed array of
+ * ATTN_NOALLOC_SCRATCH_BYTES (32 MiB) inside the library.  It calls no
+ * cudaMalloc / cudaFree / pool allocation, and encodes its tensor maps per
+ * call instead of caching them.
+ *   - Footprint: the array belongs to the library's device module, so each
+ *     GPU holds the 32 MiB from the moment that module is loaded there --
+ *     with lazy module loading (the CUDA default) at the first
+ *     attn_fwd_noalloc call on the GPU, with CUDA_MODULE_LOADING=EAGER when
+ *     the process creates its context on the GPU, even if this entry point
+ *     is never called -- until the process exits.
  *   - A plan needing more scratch returns ATTN_ERR_SCRATCH_LIMIT and launches
  *     nothing (attn_fwd runs any size).
- *   - The first call on each device looks up the array's device address
- *     (cudaGetSymbolAddress); make that first call before any stream capture.
- *   - All calls share the one array.  Calls that may overlap on the GPU
- *     (different streams, or different host threads) race on it; order them
- *     on one stream.  Each call clears the counters it needs at zero.
+ *   - Set-up: the first call on each device (any shape) looks up the array's
+ *     device address (cudaGetSymbolAddress) with that device current; make
+ *     that first call before any stream capture.
+ *   - All calls share the one array, which keeps the last call's contents.
+ *     Calls that may overlap on the GPU (different streams, or different
+ *     host threads) race on it; order them on one stream.  Each call clears
+ *     the counters it needs at zero before its kernel.
  * No counterpart in the reference: its launchers allocate nothing beyond
  * the caller's tensors (tuning/attn_test.cu:1583-1663) and have no key split.
  */
