@@ -54,6 +54,19 @@ def max_over_ranks(value: float, device=None) -> float:
     return float(t.item())
 
 
+def gather_over_ranks(value: float, device=None) -> list[float]:
+    """Every rank's value of a per-rank float, in rank order, on every rank
+    ([value] when torch.distributed is not initialised)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [float(value)]
+    t = torch.zeros(dist.get_world_size(), dtype=torch.float64, device=device)
+    t[dist.get_rank()] = float(value)
+    dist.all_reduce(t)
+    return [float(x) for x in t.tolist()]
+
+
 def sum_over_ranks(value: int, device=None) -> int:
     import torch
     import torch.distributed as dist

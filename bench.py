@@ -67,13 +67,27 @@ def parse():
                          "point-to-point and report its time separately")
     ap.add_argument("--preroll-s", type=float, default=0.5,
                     help="untimed back-to-back launches before timing (clock warm-up)")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="skip the sub-records (C4/C5 strong scaling at every N, C3 at N=1)")
     a = ap.parse_args()
-    # Fastest tile measured on B200 per workload (BM x BN sweep): 256 x 128,
-    # except D = 64 where 256 x 96 keeps two S buffers per Q tile in TMEM.
-    best = {"c3": (256, 96)}.get(a.workload, (256, 128))
+    best = best_tile(a.workload)
     a.bm = best[0] if a.bm is None else a.bm
     a.bn = best[1] if a.bn is None else a.bn
     return a
+
+
+def best_tile(wl):
+    """Fastest tile measured on B200 per workload (BM x BN sweep): 256 x 128,
+    except D = 64 where 256 x 96 keeps two S buffers per Q tile in TMEM."""
+    return {"c3": (256, 96)}.get(wl, (256, 128))
+
+
+# Sub-records of every line of our arm: the sharded configurations C4 and C5
+# (strong scaling: the whole job split over the N GPUs), and C3 at N = 1.
+# Timed steps per sub-record: a few tens to a few hundreds of ms at N = 1.
+SUB_STEPS = {"c3": 50, "c4": 10, "c5": 4}
+SUB_WARMUP = 3
+SUB_PREROLL_S = 0.3
 
 
 def peaks():
@@ -254,89 +268,159 @@ def run_reference_arm(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+class Ctx:
+    """This rank's place in the job: rank, world size, device, barrier."""
+
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+
+def measure(ctx, wl, bm, bn, steps, warmup, preroll_s, seed, keep_sets=False):
+    """Times exactly `steps` launches of workload `wl` on this rank's (batch,
+    head) units, between CUDA events on the launching stream, with a barrier
+    and a synchronize on both sides; the job time is the MAX over ranks.
+    Inputs rotate over enough sets to exceed the L2 (or one set when a set is
+    already larger).  Every rank takes the same collective steps."""
+    import torch
+    import attnprofile_b200 as ap
+    from attnprofile_b200 import shard
+    n = ctx.world
+    w = WORKLOADS[wl]
+    S, D, H = w["S"], w["D"], w["H"]
+    tdt = torch.float16 if w["dtype"] == "f16" else torch.bfloat16
+    B = w["B"] * n if w["scaling"] == "weak" else w["B"]
+    units_total = B * H
+    u0, u1 = shard.shard_range(units_total, n, ctx.rank)
+    units = u1 - u0
+    set_bytes = 4 * units * S * D * 2
+    n_sets = 1 if set_bytes >= L2_BYTES else min(4, max(2, math.ceil(2 * L2_BYTES / set_bytes)))
+    # Seeded inputs, generated per global unit so a unit's data does not
+    # depend on the number of GPUs.
+    sets = [shard.generate_units(u0, u1, S, D, tdt, ctx.dev, seed, si, w["sigma"])
+            for si in range(n_sets)]
+    torch.cuda.synchronize()
+
+    def launch(i):
+        if units:
+            Q, K, V, O = sets[i % n_sets]
+            ap.attn(Q, K, V, O, BM=bm, BN=bn)
+
+    for i in range(max(warmup, 3)):
+        launch(i)
+    torch.cuda.synchronize()
+    rc, site = ap.get_status(ctx.local)
+    if rc != 0:
+        raise SystemExit(f"{wl}: device status after warm-up: {rc} site {site:#x}")
+
+    sampler = ClockSampler(ctx.local)
+    sampler.start()
+    t_end = time.perf_counter() + preroll_s
+    i = 0
+    while time.perf_counter() < t_end:
+        launch(i)
+        i += 1
+        if i % 16 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for i in range(steps):
+        launch(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ctx.barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    rc, site = ap.get_status(ctx.local)
+    if rc != 0:
+        raise SystemExit(f"{wl}: device status after timing: {rc} site {site:#x}")
+    ms_max = shard.max_over_ranks(ms, ctx.dev)
+    out = {"ms": ms, "ms_max": ms_max, "units": units, "units_total": units_total, "S": S,
+           "D": D, "n_sets": n_sets, "set_bytes": set_bytes, "clocks": clocks, "tdt": tdt,
+           "launches": shard.sum_over_ranks(steps if units else 0, ctx.dev)}
+    if keep_sets:
+        out["sets"] = sets
+    else:
+        del sets
+        torch.cuda.empty_cache()
+    return out
+
+
+def sub_record(ctx, wl, args):
+    """One sub-record: workload `wl` on its best tile, timed like the main
+    line; value = the whole job's FLOPs / the MAX over ranks of the time."""
+    from attnprofile_b200 import shard
+    bm, bn = best_tile(wl)
+    steps = SUB_STEPS[wl]
+    m = measure(ctx, wl, bm, bn, steps, SUB_WARMUP, SUB_PREROLL_S, args.seed)
+    S, D = m["S"], m["D"]
+    achieved = flops(m["units"], S, D) / (m["ms"] / steps * 1e-3) / 1e12 if m["units"] else 0.0
+    clk = m["clocks"] or {}
+    reasons = clk.get("reasons") or []
+    bits = sum(1 << k for k, nm in enumerate(("hw_slowdown", "hw_thermal_slowdown",
+                                              "sw_thermal_slowdown", "sw_power_cap"))
+               if nm in reasons)
+    per_rank = [shard.gather_over_ranks(x, ctx.dev) for x in
+                (m["units"], achieved, m["ms"], clk.get("sm_mhz") or 0.0, float(bits))]
+    ns = argparse.Namespace(bm=bm, bn=bn, seed=args.seed)
+    cfg = config_of(wl, ns, ctx.world)
+    cfg["l2"] = (f"{m['n_sets']} rotating input sets vs 126 MiB L2" if m["n_sets"] > 1
+                 else "inputs larger than the 126 MiB L2")
+    names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    return {
+        "value": flops(m["units_total"], S, D) * steps / (m["ms_max"] * 1e-3) / 1e12,
+        "unit": "TFLOP/s", "scaling": WORKLOADS[wl]["scaling"], "n_gpus": ctx.world,
+        "steps": steps, "warmup": SUB_WARMUP, "ms_per_step": m["ms_max"] / steps,
+        "dtype": WORKLOADS[wl]["dtype"], "config": cfg,
+        "units_per_gpu": [int(x) for x in per_rank[0]],
+        "achieved_per_rank": per_rank[1], "ms_per_rank": per_rank[2],
+        "gpu_launches": m["launches"],
+        "clocks": clk,
+        "sm_mhz_per_rank": per_rank[3],
+        "reasons_per_rank": [[nm for k, nm in enumerate(names) if int(b) >> k & 1]
+                             for b in per_rank[4]],
+    }
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference_arm(args)
 
     import torch
-    import torch.distributed as dist
     import attnprofile_b200 as ap
     from attnprofile_b200 import shard
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    n = world
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
+    ctx = Ctx()
+    n, rank, dev = ctx.world, ctx.rank, ctx.dev
     w = WORKLOADS[args.workload]
     cfg = config_of(args.workload, args, n)
-    S, D, H = w["S"], w["D"], w["H"]
-    tdt = torch.float16 if w["dtype"] == "f16" else torch.bfloat16
-    units_total = cfg["B"] * H
-    u0, u1 = shard.shard_range(units_total, n, rank)
-    units = u1 - u0
+    m = measure(ctx, args.workload, args.bm, args.bn, args.steps, args.warmup, args.preroll_s,
+                args.seed, keep_sets=True)
+    S, D = m["S"], m["D"]
+    units, units_total, sets, n_sets = m["units"], m["units_total"], m["sets"], m["n_sets"]
+    tdt, ms, ms_max, clocks = m["tdt"], m["ms"], m["ms_max"], m["clocks"]
     elt = 2
-    set_bytes = 4 * units * S * D * elt
-    n_sets = 1 if set_bytes >= L2_BYTES else min(4, max(2, math.ceil(2 * L2_BYTES / set_bytes)))
-
-    # Seeded inputs, generated per global unit so a unit's data does not depend
-    # on the number of GPUs.
-    def gen_set(s):
-        return shard.generate_units(u0, u1, S, D, tdt, dev, args.seed, s, w["sigma"])
-
-    sets = [gen_set(s) for s in range(n_sets)]
-    torch.cuda.synchronize()
-
-    def launch(i):
-        Q, K, V, O = sets[i % n_sets]
-        ap.attn(Q, K, V, O, BM=args.bm, BN=args.bn)
-
-    for i in range(max(args.warmup, 3)):
-        launch(i)
-    torch.cuda.synchronize()
-    rc, site = ap.get_status(local)
-    if rc != 0:
-        raise SystemExit(f"device status after warm-up: {rc} site {site:#x}")
-
-    sampler = ClockSampler(local)
-    sampler.start()
-    t_end = time.perf_counter() + args.preroll_s
-    i = 0
-    while time.perf_counter() < t_end:
-        launch(i)
-        i += 1
-        if i % 64 == 0:
-            torch.cuda.synchronize()
-    torch.cuda.synchronize()
-
     stream = torch.cuda.current_stream()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    for i in range(args.steps):
-        launch(i)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1)
-    rc, site = ap.get_status(local)
-    if rc != 0:
-        raise SystemExit(f"device status after timing: {rc} site {site:#x}")
-
-    ms_max = shard.max_over_ranks(ms, dev)
     total_flops = flops(units_total, S, D) * args.steps
     value = total_flops / (ms_max * 1e-3) / 1e12
 
@@ -385,7 +469,8 @@ def main():
                     s_cmp.wait_event(ev_in[b])
                     if i >= 2:
                         s_cmp.wait_event(ev_out[b])  # O of buffer b read back
-                    ap.attn(Qd, Kd, Vd, Od, BM=args.bm, BN=args.bn, stream=s_cmp)
+                    if units:
+                        ap.attn(Qd, Kd, Vd, Od, BM=args.bm, BN=args.bn, stream=s_cmp)
                     ev_cmp[b].record(s_cmp)
                 with torch.cuda.stream(s_d2h):
                     s_d2h.wait_event(ev_cmp[b])
@@ -394,14 +479,14 @@ def main():
 
         e2e_steps(2)
         torch.cuda.synchronize()
-        barrier()
+        ctx.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s_h2d)
         e2e_steps(steps_e)
         s_h2d.wait_stream(s_d2h)
         e1.record(s_h2d)
         torch.cuda.synchronize()
-        barrier()
+        ctx.barrier()
         te = shard.max_over_ranks(e0.elapsed_time(e1), dev)
         e2e = {"value": flops(units_total, S, D) * steps_e / (te * 1e-3) / 1e12,
                "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * Q0.numel() * elt,
@@ -410,7 +495,7 @@ def main():
                "pipelining": "2 buffer sets, H2D / compute / D2H streams"}
         del dbuf, hq, ho
 
-    launches = shard.sum_over_ranks(args.steps, dev)
+    launches = m["launches"]
 
     # Optional consumer-side step, outside the metric: the last step's O
     # shards gathered on rank 0 (NVLink point-to-point through NCCL).
@@ -419,7 +504,7 @@ def main():
         O_last = sets[(args.steps - 1) % n_sets][3]
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         for rep in range(2):  # the first call sets up NCCL's point-to-point channels
-            barrier()
+            ctx.barrier()
             torch.cuda.synchronize()
             g0.record(stream)
             shard.gather_output(O_last, units_total, dst=0)
@@ -429,12 +514,25 @@ def main():
         g_bytes = units_total * S * D * elt * (n - 1) // n
         gather = {"ms": g_ms, "bytes_to_rank0": g_bytes, "GB_per_s": g_bytes / (g_ms * 1e-3) / 1e9,
                   "how": "torch.distributed send / batch_isend_irecv (NCCL) into rank 0's [1, B*H, S, D]"}
+    del sets, m
+    torch.cuda.empty_cache()
+
+    # Sub-records, after the main line's timing: the sharded configurations
+    # (C4, C5) strong-scaled over the N GPUs, and C3 on one GPU.
+    subs = {}
+    if not args.no_sub:
+        for wl in ("c4", "c5"):
+            if wl != args.workload:
+                subs.setdefault("sharded", {})[wl] = sub_record(ctx, wl, args)
+        if n == 1 and args.workload != "c3":
+            subs["c3"] = sub_record(ctx, "c3", args)
 
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_reference(args.workload)
 
     if rank == 0:
+        set_bytes = 4 * units * S * D * elt
         cfg["l2"] = (f"{n_sets} rotating input sets ({n_sets * set_bytes / 2**20:.0f} MiB) vs "
                      f"126 MiB L2" if n_sets > 1 else "inputs larger than the 126 MiB L2")
         pub = PUBLISHED.get(args.workload)
@@ -452,10 +550,12 @@ def main():
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
         }
+        line.update(subs)
         if gather is not None:
             line["gather"] = gather
         print(json.dumps(line), flush=True)
-    if world > 1:
+    if n > 1:
+        import torch.distributed as dist
         dist.destroy_process_group()
     return 0
 
