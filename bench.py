@@ -11,7 +11,11 @@ batch is B=N and each GPU owns its (batch, head) units -- no collective on the
 data path (weak scaling).  C4/C5 are the strong-scaling sharded shapes.
 
 Metric: attn fwd TFLOP/s = 4*B*H*S^2*D / t, whole job, t = max over ranks of
-the device time (CUDA events) of exactly K steps.  `e2e` repeats the metric
+the device time (CUDA events) of exactly K steps.  Every line of our arm also
+carries sub-records timed the same way in the same run: `sharded.c4` and
+`sharded.c5`, the sharded configurations strong-scaled over the N GPUs
+(aggregate TFLOP/s, per-rank units, achieved TFLOP/s and SM clocks), and at
+N = 1 `c3` (D = 64).  `e2e` repeats the metric
 through the public API with pinned host buffers and the H2D/D2H copies inside
 the timed region.  `cpu_baseline` times the reference's own host attention
 (oracle/_ref, the reference's verify_attn compiled from its sources) on this
