@@ -16,10 +16,14 @@ reference (tuning/solver.py:14-132):
   * BN a multiple of 32 in [32, 256] (32-column softmax chunks, TMA box <= 256);
   * tensor memory: NQ * NSBUF * BN + NQ * HD <= 512 columns, NSBUF = 2 when
     one Q tile and the doubled S buffer fit, else 1;
-  * shared memory: Q tiles + STAGES K/V slots (STAGES = 2 * NumSmem, the
-    driver's mapping) + barriers + alignment slack <= SmemLimit;
-  * registers are not a constraint (fixed split per variant): the estimate is
-    reported as 240 so the harness keeps one consumer-register setting.
+  * shared memory: Q tiles + STAGES K/V slots + barriers + alignment slack
+    <= SmemLimit, with STAGES the ring depth the library ships for the tile
+    (lib_stages, the mirror of auto_stages in csrc/attn_host.cuh: the deepest
+    ring of at most 8 slots that fits; NumSmem does not change it, as in the
+    driver's runAttn);
+  * registers are not modelled (fixed split per variant): every register
+    field is reported as 240 so the harness keeps one consumer-register
+    setting, and each solution says so with "RegsModelled": False.
 """
 from __future__ import annotations
 
@@ -45,16 +49,38 @@ def smem_bytes(BM: int, BN: int, HD: int, stages: int) -> int:
     return off_misc + 16 + 1024
 
 
+def lib_stages(BM: int, BN: int, HD: int, cap: int = 8) -> int:
+    """K/V ring depth of the library's variant (mirrors auto_stages in
+    csrc/attn_host.cuh): the deepest ring of at most `cap` slots that fits one
+    CTA's shared memory, or half the SM's for the variants built for two CTAs
+    per SM (one Q tile, BN <= 64).  0 if not even two slots fit."""
+    nq = BM // MMA_M_B200
+    limit = 233472 // 2 - 1024 if (nq == 1 and BN <= 64) else 232_448
+    nsbuf = 2 if nq * (2 * BN + HD) <= TMEM_COLS else 1
+    exp_bound = nq == 2 and HD == 64 and nq * (2 * BN + HD) <= TMEM_COLS
+    phalves = 2 if (BN >= 64 and not exp_bound) else 1
+    bars2 = nq + 2 * 2 + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1
+    off_kv = nq * 128 * HD * 2
+    best = 0
+    for s in range(2, cap + 1):
+        bars = ((bars2 + 2 * (s - 2)) * 8 + 15) // 16 * 16
+        if off_kv + s * BN * HD * 2 + max(bars, 256) + 1024 + 16 <= limit:
+            best = s
+    return best
+
+
 def _solve(HD=64, NumSmem=2, MMA_M=64, MMA_K=16, NumConsumer=2, ElementWidth=2,
            SmemLimit=232_448, KernelIdx=2, ConsumerRegLimit=240):
     if HD not in (64, 128) or ElementWidth != 2:
         return []
-    stages = max(2, 2 * NumSmem)
     bms = [256] if KernelIdx == 3 else [128]
     solutions = []
     for BM in bms:
         for BN in range(32, 257, 32):
             if tmem_columns(BM, BN, HD) > TMEM_COLS:
+                continue
+            stages = lib_stages(BM, BN, HD)
+            if stages < 2:
                 continue
             size = smem_bytes(BM, BN, HD, stages)
             if size > SmemLimit:
@@ -76,6 +102,8 @@ def _solve(HD=64, NumSmem=2, MMA_M=64, MMA_K=16, NumConsumer=2, ElementWidth=2,
                 "CombinedRegs": regs,
                 "QKStageRegs": regs,
                 "PVStageRegs": regs,
+                "RegsModelled": False,
+                "Stages": stages,
             })
     return solutions
 

@@ -34,3 +34,22 @@ def oracle_mod():
     from oracle import oracle
     oracle.build()
     return oracle
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Reports how often the bf16 one-ulp exception of the parity checks was
+    used (tests/test_gpu_attn.py::compare) in this session."""
+    # The module can be loaded under two names (as collected, and as
+    # imported by tests/test_gpu_split.py): add both counts up.
+    mods = {id(m): m for m in (sys.modules.get("test_gpu_attn"),
+                               sys.modules.get("tests.test_gpu_attn")) if m is not None}
+    parts = [m.ULP_EXCEPTIONS for m in mods.values() if hasattr(m, "ULP_EXCEPTIONS")]
+    if not parts:
+        return
+    stats = {k: sum(p[k] for p in parts) for k in ("compared", "bf16_compared", "exceptions")}
+    stats.update({k: max(p[k] for p in parts) for k in ("max_excess", "worst_share")})
+    if stats["compared"]:
+        terminalreporter.write_line(
+            "parity: {compared} elements compared ({bf16_compared} bf16); {exceptions} passed "
+            "only through the bf16 one-ulp exception (largest |diff| {max_excess:.3g}, largest "
+            "share in one comparison {worst_share:.2e})".format(**stats))

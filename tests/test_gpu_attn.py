@@ -11,8 +11,11 @@ bf16, whose spacing is 2^-8 = 3.9e-3 for |O| in [0.5, 1).  A difference far
 below 2e-3 before rounding can land on the two sides of a rounding boundary,
 so an element may differ by one bf16 ulp of the reference value even when
 that ulp exceeds 2e-3.  Nothing larger is allowed, and the mean bound stays.
-At the benchmark shapes |O| is small and the plain 2e-3 bound holds
-(tests/test_gpu_configs.py).
+The exception is counted: compare() allows it only where |O_ref| >= 0.5 (the
+only place a bf16 ulp exceeds 2e-3) and on at most EXC_FRAC of a comparison's
+elements, and the session summary reports how many elements used it and by
+how much they passed 2e-3.  At the benchmark shapes |O| is small and the
+plain 2e-3 bound holds (tests/test_gpu_configs.py).
 """
 from pathlib import Path
 
@@ -23,6 +26,11 @@ pytestmark = pytest.mark.gpu
 
 MAX_ABS = 2e-3
 MEAN_ABS = 2e-4
+EXC_FRAC = 1e-3  # largest share of elements that may use the bf16 one-ulp exception
+# Elements compared and elements that passed only through the bf16 one-ulp
+# exception, over the session (tests/conftest.py prints it).
+ULP_EXCEPTIONS = {"compared": 0, "bf16_compared": 0, "exceptions": 0, "max_excess": 0.0,
+                  "worst_share": 0.0}
 PATTERN_REL = 0.005  # scale-relative bound for the pattern case (measured worst 3.5e-4)
 TILES = [(128, 32), (128, 64), (128, 96), (128, 128), (128, 256), (256, 32), (256, 64), (256, 96),
          (256, 128)]
@@ -69,7 +77,9 @@ def bf16_ulp(x):
 
 
 def compare(oracle_mod, got_u16, ref_u16, dt):
-    """Returns (worst |diff| / allowed, mean |diff|); the first must be <= 1."""
+    """Returns (worst |diff| / allowed, mean |diff|); the first must be <= 1.
+    Elements over 2e-3 (bf16 only, within one ulp) are counted and must be
+    rare and at |O_ref| >= 0.5."""
     a = oracle_mod.to_f32(got_u16, dt).astype(np.float64)
     b = oracle_mod.to_f32(ref_u16, dt).astype(np.float64)
     assert np.isfinite(a).all()
@@ -77,6 +87,18 @@ def compare(oracle_mod, got_u16, ref_u16, dt):
     allowed = np.full_like(d, MAX_ABS)
     if dt == 1:
         allowed = np.maximum(allowed, bf16_ulp(b).astype(np.float64))
+    exc = d > MAX_ABS
+    n_exc = int(exc.sum())
+    ULP_EXCEPTIONS["compared"] += d.size
+    if dt == 1:
+        ULP_EXCEPTIONS["bf16_compared"] += d.size
+    if n_exc:
+        ULP_EXCEPTIONS["exceptions"] += n_exc
+        ULP_EXCEPTIONS["max_excess"] = max(ULP_EXCEPTIONS["max_excess"], float(d[exc].max()))
+        ULP_EXCEPTIONS["worst_share"] = max(ULP_EXCEPTIONS["worst_share"], n_exc / d.size)
+        assert dt == 1, f"{n_exc} elements over {MAX_ABS} in an f16 comparison"
+        assert np.abs(b[exc]).min() >= 0.5, "one-ulp exception used where |O_ref| < 0.5"
+        assert n_exc <= EXC_FRAC * d.size, f"{n_exc} of {d.size} elements use the ulp exception"
     return float((d / allowed).max()), float(d.mean())
 
 

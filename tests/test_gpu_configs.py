@@ -1,10 +1,16 @@
 """Parity at the benchmark configurations' full sizes (BASELINE configs C2-C5).
 
-The oracle cannot finish these shapes in seconds, so the kernel's output is
-checked on a seeded sample of query rows in every (batch, head) unit plus the
-first and last rows of the tensor, against oracle_attn_rows (the same
-restatement of tuning/utils.cuh:139-198 used everywhere else).  Tolerance:
-max-abs 2e-3, mean-abs 2e-4.
+The oracle cannot finish the whole of these shapes in seconds, so the
+kernel's output is checked on
+  * a seeded sample of query rows in every (batch, head) unit (16 per unit at
+    C4 and C5, 24 at C2 and C3) plus the first and last rows of the tensor,
+  * whole (batch, head) units: two of C4 (8192 x 8192 each) and one head of
+    C5 (32768 rows against 32768 keys, 256 key tiles of N(0, 0.5^2) inputs:
+    the long online-softmax chain),
+against oracle_attn_rows / oracle_attn (the same restatement of
+tuning/utils.cuh:139-198 used everywhere else).  Tolerance: max-abs 2e-3,
+mean-abs 2e-4, with no exception for bf16 (C4): the count of elements over
+2e-3 is reported and must be zero.
 """
 import numpy as np
 import pytest
@@ -28,7 +34,17 @@ def gen(shape, dtype, seed, sigma):
     return (torch.randn(*shape, generator=g, device="cuda") * sigma).to(dtype)
 
 
-def check_rows(engine, oracle_mod, B, H, S, D, dtype, sigma, BM, BN, rows_per_unit, seed):
+def _diff(oracle_mod, got, ref, dt, what):
+    a, b = oracle_mod.to_f32(got, dt), oracle_mod.to_f32(ref, dt)
+    assert np.isfinite(a).all()
+    d = np.abs(a.astype(np.float64) - b.astype(np.float64))
+    over = int((d > MAX_ABS).sum())
+    assert over == 0 and d.mean() <= MEAN_ABS, (what, over, float(d.max()), float(d.mean()))
+    return d.size
+
+
+def check_rows(engine, oracle_mod, B, H, S, D, dtype, sigma, BM, BN, rows_per_unit, seed,
+               full_units=()):
     torch = _torch()
     Q, K, V = (gen((B, H, S, D), dtype, seed + i, sigma) for i in range(3))
     O = engine.attn(Q, K, V, BM=BM, BN=BN)
@@ -46,13 +62,15 @@ def check_rows(engine, oracle_mod, B, H, S, D, dtype, sigma, BM, BN, rows_per_un
     q, k, v, o = u16(Q), u16(K), u16(V), u16(O)
     del Q, K, V, O
     ref = oracle_mod.attention_rows(q, k, v, rows, bn_tile=BN, dtype=dt)
-    got = o.reshape(-1, D)[rows]
-    a, b = oracle_mod.to_f32(got, dt), oracle_mod.to_f32(ref, dt)
-    assert np.isfinite(a).all()
-    d = np.abs(a - b)
-    assert d.max() <= MAX_ABS and d.mean() <= MEAN_ABS, (float(d.max()), float(d.mean()))
+    _diff(oracle_mod, o.reshape(-1, D)[rows], ref, dt, "sampled rows")
+    # whole (batch, head) units
+    qf, kf, vf, of = (x.reshape(U, 1, S, D) for x in (q, k, v, o))
+    for u in full_units:
+        sl = slice(u, u + 1)
+        ref_u = oracle_mod.attention(qf[sl], kf[sl], vf[sl], bn_tile=BN, dtype=dt)
+        _diff(oracle_mod, of[sl], ref_u, dt, f"unit {u}")
     # no NaN / Inf anywhere in the full output
-    assert np.isfinite(oracle_mod.to_f32(o[:: max(1, o.shape[0] // 4)], dt)).all()
+    assert np.isfinite(oracle_mod.to_f32(o, dt)).all()
 
 
 @pytest.mark.parametrize("BM,BN", [(256, 128), (128, 128), (128, 256), (256, 64), (512, 128)])
@@ -61,17 +79,22 @@ def test_c2_f16_d128(engine, oracle_mod, BM, BN):
     check_rows(engine, oracle_mod, 1, 16, 4096, 128, torch.float16, 1.0, BM, BN, 24, 100)
 
 
-@pytest.mark.parametrize("BM,BN", [(256, 128), (128, 128)])
+@pytest.mark.parametrize("BM,BN", [(256, 128), (256, 96), (128, 128)])
 def test_c3_f16_d64(engine, oracle_mod, BM, BN):
     torch = _torch()
     check_rows(engine, oracle_mod, 1, 16, 4096, 64, torch.float16, 1.0, BM, BN, 24, 200)
 
 
 def test_c4_bf16_d128(engine, oracle_mod):
+    """C4 in bf16: 16 rows of every one of the 256 units, and units 0 and 255
+    (the first and last (batch, head)) in full."""
     torch = _torch()
-    check_rows(engine, oracle_mod, 8, 32, 8192, 128, torch.bfloat16, 1.0, 256, 128, 2, 300)
+    check_rows(engine, oracle_mod, 8, 32, 8192, 128, torch.bfloat16, 1.0, 256, 128, 16, 300,
+               full_units=(0, 255))
 
 
 def test_c5_f16_long(engine, oracle_mod):
+    """C5: 16 rows of every head, and head 37 in full."""
     torch = _torch()
-    check_rows(engine, oracle_mod, 1, 64, 32768, 128, torch.float16, 0.5, 256, 128, 2, 400)
+    check_rows(engine, oracle_mod, 1, 64, 32768, 128, torch.float16, 0.5, 256, 128, 16, 400,
+               full_units=(37,))

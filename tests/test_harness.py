@@ -22,7 +22,9 @@ import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
 HARNESS = ROOT / "attnprofile_b200" / "harness"
-REF_TUNING = Path("/root/reference/tuning")
+# The reference checkout: $ATTNPROF_REF, else a `reference` directory beside
+# this repository; the tests that need it skip when it is absent.
+REF_TUNING = Path(os.environ.get("ATTNPROF_REF") or (ROOT.parent / "reference")) / "tuning"
 
 
 def _solver():
@@ -40,6 +42,7 @@ def test_solver_matches_library_geometry(engine):
     for D in (64, 128):
         for BM, BN in engine.SUPPORTED_TILES:
             q = engine.query_config(D, BM, BN, 0)
+            assert solver.lib_stages(BM, BN, D) == q["stages"]
             assert solver.smem_bytes(BM, BN, D, q["stages"]) == q["smem_bytes"]
             assert solver.tmem_columns(BM, BN, D) <= q["tmem_cols"]
 
@@ -63,8 +66,13 @@ def test_solver_keys_and_constraints():
         assert sols
         for s in sols:
             assert s["BN"] % 32 == 0 and s["SmemSize"] <= 232448 and s["TmemCols"] <= 512
+            assert s["RegsModelled"] is False and s["Stages"] == solver.lib_stages(
+                s["BM"], s["BN"], 128)
             assert (s["RepeatN"] == 1) == (k != 3)
             assert (s["NumSmemP"] == 0) == (k == 1)
+        # the ring depth is the library's whatever NumSmem says (runAttn ignores it)
+        assert [x["SmemSize"] for x in solver.solve(HD=128, NumSmem=1, KernelIdx=k)] == \
+            [x["SmemSize"] for x in sols]
     # BM = 256 with BN = 256 at D = 128 needs 768 TMEM columns: never proposed
     assert all(s["BN"] <= 128 for s in solver.solve(HD=128, NumSmem=1, KernelIdx=3))
 
