@@ -18,7 +18,7 @@ __all__ = [
     "AttnError", "attn", "attn_padded", "attn_profiled", "query_config", "get_status",
     "set_timeout_ns", "debug_fault", "lib", "build", "ERR", "SUPPORTED_TILES", "PAIR_TILES",
     "attn_sharded",
-    "shard_range",
+    "shard_range", "set_split", "set_schedule", "plan_split", "plan_schedule", "query_split",
 ]
 
 ERR = {
@@ -74,12 +74,17 @@ def lib() -> ctypes.CDLL:
         L.attn_debug_fault.argtypes = [i]
         ll, llp = ctypes.c_longlong, ctypes.POINTER(ctypes.c_longlong)
         L.attn_set_split.argtypes = [i]
+        L.attn_set_schedule.argtypes = [i]
+        L.attn_plan_schedule.argtypes = [ll, i, ll, ctypes.POINTER(i), llp, ctypes.POINTER(i),
+                                         ctypes.POINTER(ctypes.c_double),
+                                         ctypes.POINTER(ctypes.c_double)]
         L.attn_plan_split.argtypes = [ll, i, ll, i, ctypes.POINTER(i), llp, llp]
         L.attn_query_split.argtypes = [i, i, i, i, i, i, i, ctypes.POINTER(i), llp, llp, u64p]
         for name in ("attn_fwd", "attn_fwd_padded", "attn_fwd_profiled", "attn_fwd_sharded",
                      "attn_shard_range", "attn_get_status", "attn_query_config",
                      "attn_profile_layout", "attn_debug_fault", "attn_version",
-                     "attn_set_split", "attn_plan_split", "attn_query_split"):
+                     "attn_set_split", "attn_plan_split", "attn_query_split",
+                     "attn_set_schedule", "attn_plan_schedule"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -218,6 +223,26 @@ def set_split(mode: int) -> None:
     """Key split of the last wave for later launches: 0 automatic (default),
     1 never, 2..4 force that many key ranges per unit of the last wave."""
     _check(lib().attn_set_split(int(mode)), "attn_set_split")
+
+
+def set_schedule(mode: int) -> None:
+    """Schedule of later launches: 0 automatic (default), 1 classic (one CTA
+    per unit), 2 persistent wherever the tile has it (one resident CTA per
+    SM slot sharing the launch's (unit, key tile) steps)."""
+    _check(lib().attn_set_schedule(int(mode)), "attn_set_schedule")
+
+
+def plan_schedule(units: int, num_kv_tiles: int, slots: int) -> dict:
+    """The host planner alone (no GPU): the automatic choice between the
+    persistent and the classic schedule, the persistent grid and the most
+    pieces a unit is cut into, with both modelled costs."""
+    pers, ctas, pieces = ctypes.c_int(), ctypes.c_longlong(), ctypes.c_int()
+    cp, cc = ctypes.c_double(), ctypes.c_double()
+    _check(lib().attn_plan_schedule(units, num_kv_tiles, slots, ctypes.byref(pers),
+                                    ctypes.byref(ctas), ctypes.byref(pieces), ctypes.byref(cp),
+                                    ctypes.byref(cc)), "attn_plan_schedule")
+    return {"persistent": bool(pers.value), "ctas": ctas.value, "pieces": pieces.value,
+            "persistent_cost": cp.value, "classic_cost": cc.value}
 
 
 def plan_split(units: int, num_kv_tiles: int, slots: int, mode: int = 0) -> dict:

@@ -62,6 +62,10 @@ struct SplitPlan {
   long long units = 0, whole = 0, ctas = 0;
   size_t ws_bytes = 0;           // workspace for the split units (0: none)
   size_t off_ml = 0, off_cnt = 0, cnt_bytes = 0;
+  // Persistent schedule: `ctas` resident CTAs share total_steps (unit, key
+  // tile) steps evenly; split = the most pieces any unit is cut into.
+  bool persistent = false;
+  long long total_steps = 0;
 };
 
 struct LaunchOpts {
@@ -70,6 +74,7 @@ struct LaunchOpts {
   unsigned long long* prof = nullptr;
   int prof_cta = 0;
   int split = 0;                 // 0: automatic, 1: never split, k >= 2: split k ways
+  int schedule = 0;              // 0: automatic, 1: classic only, 2: persistent where built
   void* workspace = nullptr;     // caller-provided workspace (else stream-ordered pool)
   size_t workspace_bytes = 0;
   bool no_pool = false;          // never fall back to the pool: a split plan needs `workspace`
@@ -120,6 +125,90 @@ inline SplitPlan plan_split(long long units, int n_kv, long long slots, int mode
     pl.ctas = pl.whole + rem * pl.split;
   }
   return pl;
+}
+
+// Persistent schedule (variants with AttnConfig::PERSIST_OK): `grid`
+// resident CTAs, CTA c running steps [c T / grid, (c + 1) T / grid) of the
+// T = units * n_kv (unit, key tile) steps.  Cost model in key-tile periods of
+// one CTA: its steps, plus a fixed 2 (its first Q load and pipeline fill,
+// its last epilogue), plus 0.5 per item boundary inside its range (the
+// next item's first S is computed under the epilogue), plus for a range
+// that starts or ends inside a unit 1 (partial write) and 1.5 + 0.5 per
+// further piece (merge).  The grid size that minimises the model wins; the
+// classic plan (plan_split) is costed by its own model, and the persistent
+// schedule is taken when it is no slower.
+inline double persistent_cost(long long units, int n_kv, long long grid) {
+  const long long T = units * n_kv;
+  const long long steps = (T + grid - 1) / grid;
+  const long long items = (steps + n_kv - 1) / n_kv + 1;
+  double c = static_cast<double>(steps) + 2.0 + 0.5 * static_cast<double>(items - 1);
+  if (T % grid != 0 || (T / grid) % n_kv != 0) {
+    const long long pieces = std::min<long long>((n_kv + steps - 1) / steps + 1, 64);
+    c += 1.0 + 1.5 + 0.5 * static_cast<double>(pieces - 1);
+  }
+  return c;
+}
+
+inline double classic_cost(const SplitPlan& pl, int n_kv, long long slots) {
+  const long long nsplit = pl.units - pl.whole;
+  const long long full_waves = (pl.whole + slots - 1) / slots;
+  double c = static_cast<double>(full_waves) * (n_kv + 2);
+  if (pl.split > 1 && nsplit > 0) {
+    const long long waves = (nsplit * pl.split + slots - 1) / slots;
+    c = static_cast<double>(pl.whole / slots) * (n_kv + 2) +
+        static_cast<double>(waves) * ((n_kv + pl.split - 1) / pl.split + 4 + pl.split) + 3.0;
+  }
+  return c;
+}
+
+// The persistent plan for `units` units of n_kv key tiles on `slots`
+// resident CTAs: the grid size with the lowest modelled cost (grid <= T).
+inline SplitPlan plan_persistent(long long units, int n_kv, long long slots) {
+  SplitPlan pl;
+  pl.persistent = true;
+  pl.units = units;
+  pl.total_steps = units * n_kv;
+  const long long gmax = std::min<long long>(slots, pl.total_steps);
+  long long best_g = gmax;
+  double best = persistent_cost(units, n_kv, gmax);
+  for (long long g = gmax - 1; g >= 1 && g >= gmax / 2; --g) {
+    const double c = persistent_cost(units, n_kv, g);
+    if (c < best - 1e-9) {
+      best = c;
+      best_g = g;
+    }
+  }
+  pl.ctas = best_g;
+  // Units cut between CTAs, and the most pieces any of them has.
+  long long cut_units = 0;
+  int most = 1;
+  for (long long u0 = -1, c = 1; c < best_g; ++c) {
+    const long long b = c * pl.total_steps / best_g;
+    if (b % n_kv == 0) continue;
+    const long long u = b / n_kv;
+    if (u != u0) {
+      ++cut_units;
+      u0 = u;
+      const long long first = step_owner(u * n_kv, pl.total_steps, static_cast<int>(best_g));
+      const long long last = step_owner((u + 1) * n_kv - 1, pl.total_steps, static_cast<int>(best_g));
+      most = std::max<int>(most, static_cast<int>(last - first + 1));
+    }
+  }
+  pl.split = most;
+  pl.whole = units - cut_units;
+  return pl;
+}
+
+// Workspace of a persistent plan with cut units: one partial block (BM x D
+// f32) and one (max, sum) row block per CTA, one counter per (CTA, Q tile).
+inline void plan_workspace_persistent(SplitPlan* pl, int BM, int D, int NQ) {
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  if (pl->split <= 1) return;
+  const size_t g = static_cast<size_t>(pl->ctas);
+  pl->off_ml = up(g * BM * D * sizeof(float));
+  pl->off_cnt = pl->off_ml + up(g * BM * sizeof(float2));
+  pl->cnt_bytes = g * NQ * sizeof(int);
+  pl->ws_bytes = pl->off_cnt + up(pl->cnt_bytes);
 }
 
 // Workspace of a plan: partial O (pt_bytes per element), (max, sum) per row,
@@ -257,6 +346,9 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   if (BH > INT_MAX) return ATTN_ERR_INVALID_ARG;  // the grid is 1-D over work tiles
 
   auto kern = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE, PAIR>;
+  // The persistent schedule's kernel (the classic one again where the
+  // variant has no persistent schedule).
+  auto kern_p = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE, PAIR, C::PERSIST_OK>;
   // CTA pairs run as clusters of two consecutive CTAs.
   cudaLaunchAttribute cluster_attr{};
   cluster_attr.id = cudaLaunchAttributeClusterDimension;
@@ -285,7 +377,9 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
     slots = dev < 64 ? slots_of[dev].load(std::memory_order_relaxed) : 0;
     if (slots == 0) {
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
-          cudaSuccess)
+              cudaSuccess ||
+          cudaFuncSetAttribute(kern_p, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::SMEM_BYTES) != cudaSuccess)
         return ATTN_ERR_RESOURCE;
       int sms = 0, occ = 0;
       if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
@@ -312,6 +406,19 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   const int n_kv = (S + BN - 1) / BN;
   SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, PAIR ? 1 : o.split);
   plan_workspace(&plan, C::BM, D, NQ, sizeof(float));
+  // Persistent schedule: where the variant has it, the split mode is
+  // automatic (attn_set_split 0) and the schedule mode allows it; in
+  // automatic mode when its model is no slower than the classic plan's.
+  // (A CTA's steps are counted in 32 bits.)
+  if (C::PERSIST_OK && o.split == 0 && o.schedule != 1 && BH * qt > 0 &&
+      BH * qt * n_kv / slots < (1ll << 30)) {
+    SplitPlan pp = plan_persistent(BH * qt, n_kv, slots);
+    if (o.schedule == 2 ||
+        persistent_cost(BH * qt, n_kv, pp.ctas) <= classic_cost(plan, n_kv, slots)) {
+      plan_workspace_persistent(&pp, C::BM, D, NQ);
+      plan = pp;
+    }
+  }
   if (o.plan_out) *o.plan_out = plan;
   if (o.plan_only) return ATTN_OK;
   if (plan.ctas * C::CTAS > INT_MAX || qt > INT_MAX) return ATTN_ERR_INVALID_ARG;
@@ -340,10 +447,14 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   p.fault_mode = o.fault_mode;
   p.prof = o.prof;
   p.prof_cta = o.prof_cta;
+  p.grid = static_cast<int>(plan.ctas);
+  p.total_steps = plan.total_steps;
+  p.o_ptr = O;
+  p.o_head_elems = q_rows * D;
 
   uint8_t* ws = nullptr;
   bool pooled = false;
-  if (plan.split > 1) {
+  if (plan.split > 1) {  // classic key split, or units cut between persistent CTAs
     if (o.no_pool && (o.workspace == nullptr || o.workspace_bytes < plan.ws_bytes))
       return ATTN_ERR_SCRATCH_LIMIT;
     if (o.workspace != nullptr) {
@@ -360,7 +471,22 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
     p.ws_cnt = reinterpret_cast<int*>(ws + plan.off_cnt);
     if (cudaMemsetAsync(p.ws_cnt, 0, plan.cnt_bytes, stream) != cudaSuccess) rc = ATTN_ERR_CUDA;
   }
-  if (rc == ATTN_OK) {
+  if (rc == ATTN_OK && plan.persistent) {
+    // Cooperative launch: every CTA of the grid is resident at once, which
+    // the merge of a unit cut between CTAs relies on (its merging CTA waits,
+    // bounded, for pieces that other CTAs compute first).
+    cudaLaunchAttribute coop{};
+    coop.id = cudaLaunchAttributeCooperative;
+    coop.val.cooperative = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.ctas));
+    cfg.blockDim = dim3(C::NUM_THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = &coop;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern_p, mq, mk, mv, mo, p) != cudaSuccess) rc = ATTN_ERR_CUDA;
+  } else if (rc == ATTN_OK) {
     if constexpr (PAIR) {
       const cudaLaunchConfig_t cfg = launch_cfg(static_cast<unsigned>(plan.ctas * C::CTAS));
       if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mo, p) != cudaSuccess) rc = ATTN_ERR_CUDA;

@@ -62,6 +62,8 @@ enum : int {
   kSitePReady = 5,
   kSiteODone = 6,
   kSiteDrain = 7,
+  kSiteQFree = 8,
+  kSiteMerge = 9,
   kDeviceTimeoutBase = 0x7100,
 };
 
@@ -115,6 +117,17 @@ struct AttnParams {
   int fault_mode;              // 0 normal; 1 = producer never loads K/V (test of bounded waits)
   unsigned long long* prof;    // PROFILE builds: stamp buffer, may be null
   int prof_cta;                // linear CTA index to profile
+  // Persistent schedule (the kernel's PERSIST variant): the grid is `grid`
+  // CTAs that are all resident at once; CTA c runs steps
+  // [c * total_steps / grid, (c + 1) * total_steps / grid) of the sequence
+  // of (unit, key tile) steps, unit-major, as a series of items
+  // (ItemCursor).  Its workspace: ws_o / ws_ml hold one partial block per
+  // CTA, ws_cnt one counter per (CTA, Q tile).  O is stored from registers
+  // straight to o_ptr.
+  int grid;
+  long long total_steps;
+  void* o_ptr;
+  long long o_head_elems;      // elements from one (batch, head) block of O to the next
 };
 
 constexpr int kMaxSplit = 4;
@@ -126,6 +139,61 @@ constexpr int kMaxSplit = 4;
 struct WorkTile {
   int bh, q_row0, kv_lo, n, part, rank;
   long long slot;  // (split unit index) * split + part, for partial units
+};
+
+// ---------------------------------------------------------------------------
+// Persistent schedule: items of a CTA's step range
+// ---------------------------------------------------------------------------
+// The steps of a launch are (unit u, key tile k) in the order u * num_kv_tiles
+// + k; CTA c owns [floor(c T / G), floor((c + 1) T / G)), T = total steps,
+// G = grid <= T.  Its range cut at unit boundaries gives its items: at most
+// one at each end covers only part of a unit.  A unit cut between CTAs is
+// finished by the piece holding its first key tile (kMerger), which is the
+// last item of its CTA c0; every other piece (kWriter) is the first item of
+// one of the CTAs c0 + 1 .. c1, writes its partial result into that CTA's
+// workspace slot and counts in on c0's counter.
+enum : int { kWhole = 0, kMerger = 1, kWriter = 2 };
+
+struct Item {
+  int bh, q_row0, kv_lo, n, role;
+  int peer;  // kMerger: last CTA holding a piece of the unit; kWriter: the merging CTA
+};
+
+// The CTA whose range holds global step x: the largest c with
+// floor(c T / G) <= x.
+__host__ __device__ __forceinline__ int step_owner(long long x, long long T, int G) {
+  return static_cast<int>(((x + 1) * G - 1) / T);
+}
+
+struct ItemCursor {
+  long long cur, end;
+  __device__ __forceinline__ void init(int cta, const AttnParams& p) {
+    cur = static_cast<long long>(cta) * p.total_steps / p.grid;
+    end = static_cast<long long>(cta + 1) * p.total_steps / p.grid;
+  }
+  __device__ __forceinline__ bool next(Item& it, const AttnParams& p, int BM) {
+    if (cur >= end) return false;
+    const long long nkv = p.num_kv_tiles;
+    const long long u = cur / nkv;
+    const long long lo = cur - u * nkv;
+    const long long hi = lo + (end - cur) < nkv ? lo + (end - cur) : nkv;
+    it.bh = static_cast<int>(u / p.qt_per_bh);
+    it.q_row0 = static_cast<int>(u % p.qt_per_bh) * BM;
+    it.kv_lo = static_cast<int>(lo);
+    it.n = static_cast<int>(hi - lo);
+    if (lo == 0 && hi == nkv) {
+      it.role = kWhole;
+      it.peer = -1;
+    } else if (lo == 0) {
+      it.role = kMerger;
+      it.peer = step_owner((u + 1) * nkv - 1, p.total_steps, p.grid);
+    } else {
+      it.role = kWriter;
+      it.peer = step_owner(u * nkv, p.total_steps, p.grid);
+    }
+    cur += it.n;
+    return true;
+  }
 };
 
 __device__ __forceinline__ WorkTile work_tile_of(int cta, int BM, int ctas, int rank,
@@ -308,7 +376,15 @@ struct AttnConfig {
   static constexpr int K_SLOT_PERIOD = STAGES % 2 == 0 ? STAGES / 2 : STAGES;
   static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
   static constexpr int BAR_DRAIN = BAR_O_FINAL + NQ;
-  static constexpr int NUM_BARS = BAR_DRAIN + 1;
+  // Persistent schedule: the last S of an item has read Q tile i, so the
+  // next item's Q tile i may be loaded over it (one phase per item).
+  static constexpr int BAR_Q_FREE = BAR_DRAIN + 1;
+  static constexpr int NUM_BARS = BAR_Q_FREE + NQ;
+  // Variants that can run the persistent schedule: two Q tiles with one S
+  // buffer each (the next item's first S follows the last P V like any other
+  // S) and no CTA pair.  (One-tile CTAs with one S buffer, BN = 256, would
+  // spill registers in it.)
+  static constexpr bool PERSIST_OK = NSBUF == 1 && !PAIR && NQ == 2;
 
   static constexpr int OFF_MISC = OFF_BAR + ((NUM_BARS * 8 + 15) / 16) * 16;
   static constexpr int SMEM_USED = OFF_MISC + 16;
@@ -736,25 +812,29 @@ __device__ void relay_role(uint32_t sbase, const WorkTile& wt, const WaitCtx& w)
 // ----------------------------------------------------------------------------
 // Softmax warpgroup for Q tile qi (128 threads; thread row = TMEM lane)
 // ----------------------------------------------------------------------------
+// The KV steps of one item of Q tile qi: key tiles kv_lo .. kv_lo + n - 1,
+// which are steps J0 .. J0 + n - 1 of this CTA's sequence (the phases of the
+// S and P barriers follow the CTA's step count).  Leaves the row's running
+// max (raw score units) and running sum in m_run / l_run; false if a wait
+// failed (the warp then stops early).
 template <typename T, class C, bool PROFILE>
-__device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sgen,
-                             const CUtensorMap* tmO, const WorkTile& wt, const AttnParams& p,
-                             const WaitCtx& w, const Prof<PROFILE>& prof) {
-  const int q_row0 = wt.q_row0, bh = wt.bh;
+__device__ __forceinline__ bool softmax_steps(int qi, uint32_t tmem, uint32_t sbase,
+                                              const AttnParams& p, const WaitCtx& w,
+                                              const Prof<PROFILE>& prof, int kv_lo, int n,
+                                              int J0, int rank, float& m_run,
+                                              float& l_run) {
   auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
   const int wi = (threadIdx.x / 32) & 3;  // warp within the warpgroup = TMEM lane quarter
   const int lane = threadIdx.x & 31;
-  const int row = wi * 32 + lane;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(wi * 32) << 16);
   const uint32_t o_col = C::TMEM_O_COL + qi * C::D;
-  const int n = wt.n;
   const float sl2 = p.scale_log2;
   const bool rec = PROFILE && qi == 0 && wi == 0 && lane == 0;
   const bool rec1 = PROFILE && qi == 1 && wi == 0 && lane == 0;
   // P parts are signalled to the MMA issuer, in the even CTA of a pair.
   auto p_arrive = [&](uint32_t b) {
     if constexpr (C::PAIR) {
-      if (wt.rank != 0) {
+      if (rank != 0) {
         ptx::mbar_arrive_cluster(ptx::mapa_shared(b, 0));
         return;
       }
@@ -762,26 +842,28 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
     ptx::mbar_arrive(b);
   };
 
-  float m_run = -INFINITY;  // running max (raw score units)
-  float l_run = 0.f;        // running row sum of P (relative to m_run)
+  m_run = -INFINITY;  // running max (raw score units)
+  l_run = 0.f;        // running row sum of P (relative to m_run)
   bool ok = true;
 
   for (int j = 0; j < n; ++j) {
-    const int buf = j % C::NSBUF;
+    const int g = J0 + j;  // this CTA's step: barrier phases
+    const int sl = g < kProfSlots ? g : kProfSlots;  // profiler slot
+    const int buf = g % C::NSBUF;
     const uint32_t s_col = (qi * C::NSBUF + buf) * C::BN;
     ok = __all_sync(0xffffffffu,
-                    wait_bar(bar(C::BAR_S_FULL + qi * C::NSBUF + buf), (j / C::NSBUF) & 1, w,
+                    wait_bar(bar(C::BAR_S_FULL + qi * C::NSBUF + buf), static_cast<uint32_t>((g / C::NSBUF) & 1), w,
                              kSiteSFull));
     if (!ok) break;
     ptx::tc_fence_after();
     if (rec) {
-      prof.stamp(kPhQK, j, 1);
-      prof.stamp(kPhSoftmax, j, 0);
-      prof.stamp(kPhSmLoadS, j, 0);
+      prof.stamp(kPhQK, sl, 1);
+      prof.stamp(kPhSoftmax, sl, 0);
+      prof.stamp(kPhSmLoadS, sl, 0);
     }
-    if (rec1) prof.stamp(kPhSoftmaxT1, j, 0);
+    if (rec1) prof.stamp(kPhSoftmaxT1, sl, 0);
 
-    const int lim = p.S - (wt.kv_lo + j) * C::BN;  // valid key columns in this tile
+    const int lim = p.S - (kv_lo + j) * C::BN;  // valid key columns in this tile
     const int pbar = C::BAR_P_READY + (qi * C::NSBUF + buf) * C::PHALVES;
     float mx = -INFINITY;
     constexpr int KEEP = C::BN <= 128;
@@ -797,8 +879,8 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       ptx::tmem_wait_ld();
       ptx::reg_fence(sreg);
       if (rec) {
-        prof.stamp(kPhSmLoadS, j, 1);
-        prof.stamp(kPhSmMax, j, 0);
+        prof.stamp(kPhSmLoadS, sl, 1);
+        prof.stamp(kPhSmMax, sl, 0);
       }
       if (lim < C::BN) {
 #pragma unroll
@@ -836,7 +918,7 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       // place.  With one S buffer the S_FULL observed above already covers it.
       if constexpr (C::ODONE_PER_STEP) {
         ok = __all_sync(0xffffffffu,
-                        wait_bar(bar(C::BAR_O_DONE + qi), (j - 1) & 1, w, kSiteODone));
+                        wait_bar(bar(C::BAR_O_DONE + qi), static_cast<uint32_t>((g - 1) & 1), w, kSiteODone));
         if (!ok) break;
         ptx::tc_fence_after();
       }
@@ -853,8 +935,8 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
     }
 
     if (rec) {
-      prof.stamp(kPhSmMax, j, 1);
-      prof.stamp(kPhSmExp, j, 0);
+      prof.stamp(kPhSmMax, sl, 1);
+      prof.stamp(kPhSmExp, sl, 0);
     }
     // P = exp2(s * scale_log2 - m * scale_log2), packed to T pairs over S.
     const float neg = -m_run * sl2;
@@ -901,8 +983,8 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) p_arrive(bar(pbar));
-        if (rec) prof.stamp(kPhPFirst, j, 0);
-        if (rec1) prof.stamp(kPhPFirst, j, 1);
+        if (rec) prof.stamp(kPhPFirst, sl, 0);
+        if (rec1) prof.stamp(kPhPFirst, sl, 1);
       }
     }
     float sa, sb, sc_, sd;
@@ -910,18 +992,41 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
     ptx::f2_unpack(part[1], sc_, sd);
     const float sum = (sa + sb) + (sc_ + sd);
     if (rec) {
-      prof.stamp(kPhSmExp, j, 1);
-      prof.stamp(kPhSmStoreP, j, 0);
+      prof.stamp(kPhSmExp, sl, 1);
+      prof.stamp(kPhSmStoreP, sl, 0);
     }
     ptx::tmem_wait_st();
-    if (rec) prof.stamp(kPhSmStoreP, j, 1);
+    if (rec) prof.stamp(kPhSmStoreP, sl, 1);
     ptx::tc_fence_before();
     __syncwarp();
     if (lane == 0) p_arrive(bar(pbar + C::PHALVES - 1));
-    if (rec) prof.stamp(kPhSoftmax, j, 1);
-    if (rec1) prof.stamp(kPhSoftmaxT1, j, 1);
+    if (rec) prof.stamp(kPhSoftmax, sl, 1);
+    if (rec1) prof.stamp(kPhSoftmaxT1, sl, 1);
     l_run = l_run * alpha + sum;
   }
+  return ok;
+}
+
+// The classic schedule: one work tile per CTA, the softmax steps of it, then
+// its epilogue (TMA store of O through the Q tile's shared memory, or the
+// partial write / merge of a key split).
+template <typename T, class C, bool PROFILE>
+__device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sgen,
+                             const CUtensorMap* tmO, const WorkTile& wt, const AttnParams& p,
+                             const WaitCtx& w, const Prof<PROFILE>& prof) {
+  const int q_row0 = wt.q_row0, bh = wt.bh;
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  const int wi = (threadIdx.x / 32) & 3;  // warp within the warpgroup = TMEM lane quarter
+  const int lane = threadIdx.x & 31;
+  const int row = wi * 32 + lane;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(wi * 32) << 16);
+  const uint32_t o_col = C::TMEM_O_COL + qi * C::D;
+  const float sl2 = p.scale_log2;
+  const bool rec = PROFILE && qi == 0 && wi == 0 && lane == 0;
+
+  float m_run, l_run;
+  bool ok = softmax_steps<T, C, PROFILE>(qi, tmem, sbase, p, w, prof, wt.kv_lo, wt.n, 0, wt.rank,
+                                         m_run, l_run);
 
   // Epilogue: wait for the last P V, normalise, stage in the Q slot, TMA store.
   // Every warp of the group reaches both named barriers, also after a failed
@@ -1156,7 +1261,487 @@ __device__ void observer_role(uint32_t sbase, int n, const WaitCtx& w, const Pro
   }
 }
 
-template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE, bool PAIR = false>
+// ============================================================================
+// Persistent schedule (the PERSIST kernel variant): every CTA runs its step range
+// as a series of items (ItemCursor), all three roles walking the same items.
+// The K/V ring, the S and P barriers run on the CTA's step count J, so a new
+// item's first S follows the previous item's last P V like any other S; the
+// Q, O_FINAL and Q_FREE barriers complete one phase per item.  The next
+// item's Q tiles are loaded as soon as the current item's last S has read
+// them (Q_FREE), so its first S is computed while the softmax warps finish
+// the current item; O goes from registers straight to global memory.
+// ============================================================================
+
+// Producer: Q of the first item, K_0, then per step V_J and K_{J+1}; at an
+// item's last step the next item's Q tiles (after Q_FREE) and its K_0.
+template <class C, bool PROFILE>
+__device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* tmK,
+                                     const CUtensorMap* tmV, uint32_t sbase, const AttnParams& p,
+                                     const WaitCtx& w, const Prof<PROFILE>& prof) {
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  const uint64_t pol_kv = ptx::l2_policy_evict_last();
+  const uint64_t pol_q = ptx::l2_policy_evict_first();
+  ItemCursor cur;
+  cur.init(blockIdx.x, p);
+  Item it, nx;
+  if (!cur.next(it, p, C::BM)) return;
+  bool has_nx = cur.next(nx, p, C::BM);
+
+  int q_item = 0;  // the item whose Q load is the latest issued
+  auto load_q = [&](const Item& x) {
+#pragma unroll
+    for (int i = 0; i < C::NQ; ++i) {
+      ptx::mbar_arrive_expect_tx(bar(C::BAR_Q + i), C::Q_TILE_BYTES);
+#pragma unroll
+      for (int d = 0; d < C::DBLK; ++d)
+        ptx::tma_load_3d_hint(sbase + C::OFF_Q + i * C::Q_TILE_BYTES + d * C::Q_BLK_BYTES, tmQ,
+                              bar(C::BAR_Q + i), d * 64, x.q_row0 + i * C::QROWS, x.bh, pol_q);
+    }
+  };
+  prof.stamp(kPhLoadQ, 0, 0);
+  load_q(it);
+  if (p.fault_mode == 1) return;  // test hook: K/V never arrive; consumers time out
+
+  long long t = 0;  // ring item counter: K_J is item 2J, V_J item 2J + 1
+  long long last_issued[C::STAGES];
+#pragma unroll
+  for (int s = 0; s < C::STAGES; ++s) last_issued[s] = -1;
+  bool ok = true;
+
+  // k_bar >= 0: the K load completes on that slot's FULL barrier (armed by
+  // the V item just before it for both tiles' bytes); its own gets a plain
+  // arrival to keep its phase count.
+  auto produce = [&](bool is_k, const Item& x, int j, long long J, bool joint, int k_bar) {
+    const int s = static_cast<int>(t % C::STAGES);
+    if (t >= C::STAGES) {
+      uint32_t eb, par;
+      if constexpr (C::V_RELEASE_WITH_K) {
+        const long long m = (t - C::STAGES + 1) / 2;  // the K item whose commit frees slot s
+        eb = bar(C::BAR_KV_EMPTY + static_cast<int>((2 * m) % C::STAGES));
+        par = static_cast<uint32_t>((m / C::K_SLOT_PERIOD) & 1);
+      } else {
+        eb = bar(C::BAR_KV_EMPTY + s);
+        par = static_cast<uint32_t>((t / C::STAGES - 1) & 1);
+      }
+      if (!wait_bar(eb, par, w, kSiteKvEmpty)) {
+        ok = false;
+        return;
+      }
+    }
+    const int sl = J < kProfSlots ? static_cast<int>(J) : kProfSlots;
+    prof.stamp(is_k ? kPhLoadK : kPhLoadV, sl, 0);
+    uint32_t full = bar(C::BAR_KV_FULL + s);
+    if (k_bar >= 0) {
+      ptx::mbar_arrive(full);
+      full = bar(C::BAR_KV_FULL + k_bar);
+    } else {
+      ptx::mbar_arrive_expect_tx(full, joint ? 2 * C::KV_TILE_BYTES : C::KV_TILE_BYTES);
+    }
+    const uint32_t dst = sbase + C::OFF_KV + s * C::KV_TILE_BYTES;
+    const int key0 = (x.kv_lo + j) * C::BN;
+    if (is_k) {
+#pragma unroll
+      for (int d = 0; d < C::DBLK; ++d)
+        ptx::tma_load_3d_hint(dst + d * C::K_BLK_BYTES, tmK, full, d * 64, key0, x.bh, pol_kv);
+    } else {
+#pragma unroll
+      for (int d = 0; d < C::DBLK; ++d)
+        ptx::tma_load_3d_hint(dst + d * C::V_BLK_BYTES, tmV, full, d * 64, key0, x.bh, pol_kv);
+    }
+    last_issued[s] = t;
+    ++t;
+  };
+
+  produce(true, it, 0, 0, false, -1);
+  long long J = 0;
+  int item = 0;
+  while (ok) {
+    for (int j = 0; j < it.n && ok; ++j, ++J) {
+      const bool last = j == it.n - 1;
+      // V_J and K_{J+1} land together only inside an item: at an item's end
+      // the next K waits for Q_FREE, and V_J must not wait for it.
+      const bool joint = C::KV_JOINT_FULL && !last;
+      const int sv = static_cast<int>(t % C::STAGES);
+      produce(false, it, j, J, joint, -1);
+      if (!ok) break;
+      if (!last) {
+        produce(true, it, j + 1, J + 1, false, joint ? sv : -1);
+      } else if (has_nx) {
+#pragma unroll
+        for (int i = 0; i < C::NQ; ++i)
+          if (ok && !wait_bar(bar(C::BAR_Q_FREE + i), static_cast<uint32_t>(item & 1), w,
+                              kSiteQFree))
+            ok = false;
+        if (!ok) break;
+        load_q(nx);
+        q_item = item + 1;
+        produce(true, nx, 0, J + 1, false, -1);
+      }
+    }
+    if (!ok || !has_nx) break;
+    it = nx;
+    ++item;
+    has_nx = cur.next(nx, p, C::BM);
+  }
+  if (!ok) {
+    // Leave no bulk copy in flight: wait (bounded) for the latest load into
+    // every slot (a K load of a joint landing completes with the V load of
+    // the slot just before it, whose wait covers it) and for the latest Q
+    // loads.
+    const unsigned long long t0 = ptx::globaltimer_ns();
+#pragma unroll
+    for (int s = 0; s < C::STAGES; ++s) {
+      if (last_issued[s] < 0) continue;
+      const uint32_t r = static_cast<uint32_t>((last_issued[s] / C::STAGES) & 1);
+      while (!ptx::mbar_try_wait(bar(C::BAR_KV_FULL + s), r)) {
+        if (ptx::globaltimer_ns() - t0 > w.timeout_ns) break;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < C::NQ; ++i) {
+      while (!ptx::mbar_try_wait(bar(C::BAR_Q + i), static_cast<uint32_t>(q_item & 1))) {
+        if (ptx::globaltimer_ns() - t0 > w.timeout_ns) break;
+      }
+    }
+  }
+}
+
+// MMA issuer (single thread) over the CTA's items.
+template <class C, bool PROFILE>
+__device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnParams& p,
+                                    const WaitCtx& w, const Prof<PROFILE>& prof) {
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  auto signal = [&](uint32_t b) { ptx::mma_commit(b); };
+  ItemCursor cur;
+  cur.init(blockIdx.x, p);
+  Item it, nx;
+  if (!cur.next(it, p, C::BM)) return;
+  bool has_nx = cur.next(nx, p, C::BM);
+  bool ok = true;
+
+  long long t = 0;
+  auto ring_wait = [&](int& stage) -> bool {
+    stage = static_cast<int>(t % C::STAGES);
+    const bool r = wait_bar(bar(C::BAR_KV_FULL + stage),
+                            static_cast<uint32_t>((t / C::STAGES) & 1), w, kSiteKvFull);
+    ++t;
+    if (r) ptx::tc_fence_after();
+    return r;
+  };
+
+  constexpr int KSTEPS_S = C::D / 16;
+  uint64_t qd0[C::NQ];
+#pragma unroll
+  for (int i = 0; i < C::NQ; ++i)
+    qd0[i] = ptx::smem_desc_sw128(sbase + C::OFF_Q + i * C::Q_TILE_BYTES, 16, 1024);
+  const uint64_t kd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, 16, 1024);
+  const uint64_t vd0 = ptx::smem_desc_sw128(sbase + C::OFF_KV, C::V_BLK_BYTES, 1024);
+  auto slot_off = [](int stage) -> uint32_t {
+    return static_cast<uint32_t>((stage * C::KV_TILE_BYTES) >> 4);
+  };
+  auto issue_s = [&](int i, int stage) {
+    const uint32_t d_tmem = tmem + i * C::BN;
+    const uint64_t kd = ptx::desc_add(kd0, slot_off(stage));
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS_S; ++kk) {
+      const uint32_t qo = static_cast<uint32_t>(((kk >> 2) * C::Q_BLK_BYTES + (kk & 3) * 32) >> 4);
+      const uint32_t ko = static_cast<uint32_t>(((kk >> 2) * C::K_BLK_BYTES + (kk & 3) * 32) >> 4);
+      ptx::mma_ss<1>(d_tmem, ptx::desc_add(qd0[i], qo), ptx::desc_add(kd, ko), C::IDESC_S,
+                     kk > 0 ? 1u : 0u);
+    }
+  };
+  auto issue_pv = [&](int i, int stage, int k0, int k1, bool first) {
+    const uint32_t p_tmem = tmem + i * C::BN;
+    const uint32_t o_tmem = tmem + C::TMEM_O_COL + i * C::D;
+    const uint64_t vd = ptx::desc_add(vd0, slot_off(stage));
+#pragma unroll
+    for (int kk = k0; kk < k1; ++kk)
+      ptx::mma_ts<1>(o_tmem, p_tmem + kk * 8, ptx::desc_add(vd, static_cast<uint32_t>(kk * 2048 >> 4)),
+                     C::IDESC_PV, (!first || kk > 0) ? 1u : 0u);
+  };
+
+  // The first item: its Q tiles, K_0 and the S of its first step.
+#pragma unroll
+  for (int i = 0; i < C::NQ; ++i)
+    if (ok) ok = wait_bar(bar(C::BAR_Q + i), 0, w, kSiteQ);
+  if (ok) {
+    ptx::tc_fence_after();
+    prof.stamp(kPhLoadQ, 0, 1);
+    int sk;
+    if ((ok = ring_wait(sk))) {
+      prof.stamp(kPhLoadK, 0, 1);
+#pragma unroll
+      for (int i = 0; i < C::NQ; ++i) {
+        if (i == 0) prof.stamp(kPhQK, 0, 0);
+        issue_s(i, sk);
+        signal(bar(C::BAR_S_FULL + i));
+        if (it.n == 1) signal(bar(C::BAR_Q_FREE + i));
+      }
+      signal(bar(C::BAR_KV_EMPTY + sk));
+    }
+  }
+
+  constexpr int KSTEPS = C::BN / 16;
+  constexpr int KSPLIT = C::PHALVES == 2 ? 2 * C::PSPLIT_CHUNKS : KSTEPS;
+  long long J = 0;
+  int item = 0;
+  while (ok) {
+    for (int j = 0; j < it.n && ok; ++j, ++J) {
+      const bool last = j == it.n - 1;
+      const bool more = !last || has_nx;  // is there a step J + 1 in this CTA?
+      const int sl = J < kProfSlots ? static_cast<int>(J) : kProfSlots;
+      int sv;
+      prof.stamp(kPhVWait, sl, 0);
+      if (!(ok = ring_wait(sv))) break;  // V_J (and K_{J+1} when it landed with it)
+      prof.stamp(kPhVWait, sl, 1);
+      prof.stamp(kPhLoadV, sl, 1);
+      int sk = -1;
+      for (int i = 0; i < C::NQ && ok; ++i) {
+        const int pb = C::BAR_P_READY + i * C::PHALVES;
+#pragma unroll
+        for (int h = 0; h < C::PHALVES; ++h) {
+          if (h == C::PHALVES - 1 && more && sk < 0) {
+            if (C::KV_JOINT_FULL && !last) {
+              sk = static_cast<int>(t % C::STAGES);  // landed with V_J
+              ++t;
+            } else if (!(ok = ring_wait(sk))) {
+              break;
+            }
+            if (J + 1 < kProfSlots) prof.stamp(kPhLoadK, static_cast<int>(J + 1), 1);
+          }
+          if (!(ok = wait_bar(bar(pb + h), static_cast<uint32_t>(J & 1), w, kSitePReady))) break;
+          ptx::tc_fence_after();
+          if (h == 0) {
+            if (i == 0) prof.stamp(kPhPV, sl, 0);
+            prof.stamp(kPhMmaT0 + i, sl, 0);
+          }
+          issue_pv(i, sv, h == 0 ? 0 : KSPLIT, h == 0 ? KSPLIT : KSTEPS, j == 0);
+        }
+        if (!ok) break;
+        // The item's result is complete once its last P V is: O_FINAL before
+        // the next item's first S, which need not wait for the epilogue.
+        if (last) signal(bar(C::BAR_O_FINAL + i));
+        if (more) {
+          const Item& ni = last ? nx : it;
+          const int nj = last ? 0 : j + 1;
+          if (last) {
+            if (!(ok = wait_bar(bar(C::BAR_Q + i), static_cast<uint32_t>((item + 1) & 1), w,
+                                kSiteQ)))
+              break;
+            ptx::tc_fence_after();
+          }
+          if (i == 0 && J + 1 < kProfSlots) prof.stamp(kPhQK, static_cast<int>(J + 1), 0);
+          issue_s(i, sk);
+          signal(bar(C::BAR_S_FULL + i));
+          if (nj == ni.n - 1) signal(bar(C::BAR_Q_FREE + i));  // the item's last S has read Q_i
+        }
+        if (C::ODONE_PER_STEP) signal(bar(C::BAR_O_DONE + i));
+        prof.stamp(kPhMmaT0 + i, sl, 1);
+      }
+      if (!ok) break;
+      if constexpr (!C::V_RELEASE_WITH_K) signal(bar(C::BAR_KV_EMPTY + sv));
+      if (sk >= 0) signal(bar(C::BAR_KV_EMPTY + sk));  // with V_RELEASE_WITH_K: V_J's slot too
+    }
+    if (!ok || !has_nx) break;
+    it = nx;
+    ++item;
+    has_nx = cur.next(nx, p, C::BM);
+  }
+
+  // Drain: every MMA this thread issued has completed before TMEM is freed.
+  ptx::mma_commit<1>(bar(C::BAR_DRAIN));
+  const unsigned long long t0 = ptx::globaltimer_ns();
+  while (!ptx::mbar_try_wait(bar(C::BAR_DRAIN), 0)) {
+    if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
+      if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + kSiteDrain);
+      break;
+    }
+  }
+}
+
+// Softmax warpgroup of Q tile qi over the CTA's items, with each item's
+// epilogue: a whole unit stores O; a kWriter piece writes its normalised
+// partial O and (row max, row sum) into its CTA's workspace slot and counts
+// in on the merging CTA's counter; the kMerger piece waits for its unit's
+// writers, adds their partials to its own in key order and stores O.
+// Every decision that guards a named barrier is taken by all 128 threads
+// together (named_bar_and).
+template <typename T, class C, bool PROFILE>
+__device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
+                                        const AttnParams& p, const WaitCtx& w,
+                                        const Prof<PROFILE>& prof) {
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  const int wi = (threadIdx.x / 32) & 3;
+  const int lane = threadIdx.x & 31;
+  const int row = wi * 32 + lane;
+  const int rrow = qi * C::QROWS + row;  // row within the unit
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(wi * 32) << 16);
+  const uint32_t o_col = C::TMEM_O_COL + qi * C::D;
+  const float sl2 = p.scale_log2;
+  const bool rec = PROFILE && qi == 0 && wi == 0 && lane == 0;
+  const uint32_t nbar = 1 + qi;
+  constexpr int BLK = C::BM * C::D / 4;  // float4 per workspace slot
+
+  // Converts 32 values and stores them at dst (16-byte aligned).
+  auto store32 = [&](T* dst, const float* v) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u;
+      u.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+      u.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+      u.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+      u.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+      reinterpret_cast<uint4*>(dst)[q] = u;
+    }
+  };
+
+  ItemCursor cur;
+  cur.init(blockIdx.x, p);
+  Item it;
+  int J = 0;
+  int item = 0;
+  bool go = true;
+  while (go && cur.next(it, p, C::BM)) {
+    float m_run, l_run;
+    const bool ok = softmax_steps<T, C, PROFILE>(qi, tmem, sbase, p, w, prof, it.kv_lo, it.n, J,
+                                                 0, m_run, l_run);
+    J += it.n;
+    if (rec && item == 0) prof.stamp(kPhEpilogue, kEpAll, 0);
+    go = ptx::named_bar_and(nbar, 128, ok && *w.abort == 0);
+    if (!go) break;
+    if (rec && item == 0) prof.stamp(kPhEpilogue, kEpWaitO, 0);
+    bool fin = wait_bar(bar(C::BAR_O_FINAL + qi), static_cast<uint32_t>(item & 1), w, kSiteODone);
+    go = ptx::named_bar_and(nbar, 128, fin);
+    if (rec && item == 0) prof.stamp(kPhEpilogue, kEpWaitO, 1);
+    if (!go) break;
+    ptx::tc_fence_after();
+
+    const long long grow = static_cast<long long>(it.q_row0) + qi * C::QROWS + row;
+    T* orow = static_cast<T*>(p.o_ptr) + it.bh * p.o_head_elems + grow * C::D;
+    const bool store_row = grow < p.S;
+
+    if (it.role == kWriter) {
+      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpPartial, 0);
+      // Normalised partial O as float4 columns of this CTA's slot: the 32
+      // lanes of a warp (32 consecutive rows) write 512 contiguous bytes.
+      const float inv = 1.f / l_run;
+      float4* dst = p.ws_o + static_cast<long long>(blockIdx.x) * BLK + rrow;
+#pragma unroll 1
+      for (int c = 0; c < C::D / 32; ++c) {
+        uint32_t o[32];
+        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(o);
+#pragma unroll
+        for (int t4 = 0; t4 < 8; ++t4)
+          dst[(c * 8 + t4) * C::BM] = make_float4(
+              __uint_as_float(o[4 * t4 + 0]) * inv, __uint_as_float(o[4 * t4 + 1]) * inv,
+              __uint_as_float(o[4 * t4 + 2]) * inv, __uint_as_float(o[4 * t4 + 3]) * inv);
+      }
+      p.ws_ml[static_cast<long long>(blockIdx.x) * C::BM + rrow] = make_float2(m_run, l_run);
+      __threadfence();
+      ptx::named_bar_sync(nbar, 128);
+      if (row == 0) atomicAdd(p.ws_cnt + it.peer * C::NQ + qi, 1);
+      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpPartial, 1);
+    } else if (it.role == kMerger) {
+      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpCount, 0);
+      const int nw = it.peer - static_cast<int>(blockIdx.x);  // writers: the next nw CTAs
+      int* cnt = p.ws_cnt + static_cast<int>(blockIdx.x) * C::NQ + qi;
+      bool ready = true;
+      if (row == 0) {
+        const unsigned long long t0 = ptx::globaltimer_ns();
+        while (ptx::ld_acquire_gpu(cnt) < nw) {
+          if (*w.abort) {
+            ready = false;
+            break;
+          }
+          if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
+            *w.abort = 1;
+            if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + kSiteMerge);
+            ready = false;
+            break;
+          }
+        }
+        __threadfence();
+      }
+      go = ptx::named_bar_and(nbar, 128, ready);
+      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpCount, 1);
+      if (!go) break;
+      if (row == 0) *cnt = 0;  // ready for the next launch (only this CTA reads it)
+      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 0);
+      // Weights of the pieces in key order (own piece first), as the classic
+      // merge computes them: w_q = l_q 2^((m_q - m) scale), m their max.
+      float mmax = m_run;
+#pragma unroll 1
+      for (int q = 1; q <= nw; ++q)
+        mmax = fmaxf(mmax, __ldcg(p.ws_ml + static_cast<long long>(blockIdx.x + q) * C::BM + rrow).x);
+      const float w_own = l_run * ptx::ex2_approx((m_run - mmax) * sl2);
+      float tot = w_own;
+#pragma unroll 1
+      for (int q = 1; q <= nw; ++q) {
+        const float2 ml = __ldcg(p.ws_ml + static_cast<long long>(blockIdx.x + q) * C::BM + rrow);
+        tot += ml.y * ptx::ex2_approx((ml.x - mmax) * sl2);
+      }
+      const float inv_tot = 1.f / tot;
+      const float inv_own = 1.f / l_run;
+#pragma unroll 1
+      for (int c = 0; c < C::D / 32; ++c) {
+        uint32_t o[32];
+        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(o);
+        float acc[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] = w_own * (__uint_as_float(o[e]) * inv_own);
+#pragma unroll 1
+        for (int q = 1; q <= nw; ++q) {
+          const long long sq = static_cast<long long>(blockIdx.x + q);
+          const float2 ml = __ldcg(p.ws_ml + sq * C::BM + rrow);
+          const float wq = ml.y * ptx::ex2_approx((ml.x - mmax) * sl2);
+          const float4* src = p.ws_o + sq * BLK + rrow + (c * 8) * C::BM;
+          float4 v[8];
+#pragma unroll
+          for (int t4 = 0; t4 < 8; ++t4) v[t4] = __ldcg(src + t4 * C::BM);
+#pragma unroll
+          for (int t4 = 0; t4 < 8; ++t4) {
+            acc[4 * t4 + 0] = fmaf(wq, v[t4].x, acc[4 * t4 + 0]);
+            acc[4 * t4 + 1] = fmaf(wq, v[t4].y, acc[4 * t4 + 1]);
+            acc[4 * t4 + 2] = fmaf(wq, v[t4].z, acc[4 * t4 + 2]);
+            acc[4 * t4 + 3] = fmaf(wq, v[t4].w, acc[4 * t4 + 3]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] *= inv_tot;
+        if (store_row) store32(orow + c * 32, acc);
+      }
+      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 1);
+    } else {
+      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 0);
+      const float inv = 1.f / l_run;
+#pragma unroll 1
+      for (int c = 0; c < C::D / 32; ++c) {
+        uint32_t o[32];
+        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(o);
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]) * inv;
+        if (store_row) store32(orow + c * 32, v);
+      }
+      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 1);
+    }
+    if (rec && item == 0) prof.stamp(kPhEpilogue, kEpAll, 1);
+    ++item;
+  }
+}
+
+// PERSIST: the persistent schedule (AttnParams::grid and following), compiled as a
+// kernel of its own for the variants that have it (AttnConfig::PERSIST_OK),
+// so that its softmax loop and the classic one are allocated registers
+// separately.
+template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE, bool PAIR = false,
+          bool PERSIST = false>
 __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_THREADS,
                                   AttnConfig<T, D, BN, NQ, STAGES, PAIR>::MIN_CTAS_PER_SM)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -1200,6 +1785,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_TH
     for (int i = 0; i < C::NQ; ++i) {
       ptx::mbar_init(bar(C::BAR_O_DONE + i), 1);
       ptx::mbar_init(bar(C::BAR_O_FINAL + i), 1);
+      ptx::mbar_init(bar(C::BAR_Q_FREE + i), 1);
     }
     ptx::mbar_init(bar(C::BAR_DRAIN), C::NUM_ISSUERS);
     *abort_flag = 0;
@@ -1225,7 +1811,35 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_TH
   const WaitCtx w{abort_flag, p.status, p.timeout_ns};
   Prof<PROFILE> prof{(PROFILE && static_cast<int>(blockIdx.x) == p.prof_cta) ? p.prof : nullptr};
 
-  if (warp < C::NUM_SOFTMAX_WARPS) {
+  if constexpr (PERSIST) {
+    static_assert(C::PERSIST_OK, "the persistent schedule needs one S buffer per Q tile, no pair");
+    {
+      if (warp < C::NUM_SOFTMAX_WARPS) {
+        if constexpr (C::NQ == 2) ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
+        softmax_role_persistent<T, C, PROFILE>(warp / 4, tmem, sbase, p, w, prof);
+      } else {
+        if constexpr (C::NQ == 2) ptx::setmaxnreg_dec<C::REG_OTHER>();
+        if (warp == C::LOAD_WARP) {
+          if (lane == 0) load_role_persistent<C, PROFILE>(&tmQ, &tmK, &tmV, sbase, p, w, prof);
+        } else if (warp == C::MMA_WARP) {
+          if (lane == 0) mma_role_persistent<C, PROFILE>(tmem, sbase, p, w, prof);
+        } else if (warp == C::OBSERVER_WARP) {
+          if constexpr (PROFILE) {
+            // Stamps the completions of the first P Vs of tile 0 (the CTA's
+            // first item; its O_FINAL ends the watch).
+            if (lane == 0 && prof.buf != nullptr) {
+              ItemCursor c0;
+              c0.init(blockIdx.x, p);
+              Item first;
+              if (c0.next(first, p, C::BM))
+                observer_role<C>(sbase, first.n < kProfSlots ? first.n : kProfSlots, w, prof);
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp < C::NUM_SOFTMAX_WARPS) {
     if constexpr (C::NQ == 2) ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
     softmax_role<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, wt, p, w, prof);
   } else {

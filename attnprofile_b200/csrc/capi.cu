@@ -26,6 +26,7 @@ namespace {
 std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 std::atomic<int> g_fault_mode{0};
 std::atomic<int> g_split_mode{0};
+std::atomic<int> g_schedule_mode{0};
 constexpr int kMaxDev = 64;
 std::mutex g_status_mu;
 int* g_status_ptr[kMaxDev] = {};
@@ -73,6 +74,7 @@ static int run(const void* Q, const void* K, const void* V, void* O, int B, int 
   o.prof = prof;
   o.prof_cta = prof_cta;
   o.split = g_split_mode.load();
+  o.schedule = g_schedule_mode.load();
   return dispatch(Q, K, V, O, B, H, S, D, SQO, SKV, dtype, BM, BN, st, o);
 }
 
@@ -111,6 +113,7 @@ int run_in_workspace(const void* Q, const void* K, const void* V, void* O, int B
   o.timeout_ns = g_timeout_ns.load();
   o.fault_mode = g_fault_mode.load();
   o.split = split_mode;
+  o.schedule = g_schedule_mode.load();
   o.workspace = ws;
   o.workspace_bytes = ws_bytes;
   o.no_pool = true;
@@ -291,6 +294,28 @@ int attn_set_split(int mode) {
   return ATTN_OK;
 }
 
+int attn_set_schedule(int mode) {
+  if (mode < 0 || mode > 2) return ATTN_ERR_INVALID_ARG;
+  g_schedule_mode.store(mode);
+  return ATTN_OK;
+}
+
+int attn_plan_schedule(long long units, int num_kv_tiles, long long slots, int* persistent,
+                       long long* ctas, int* pieces, double* persistent_cost_out,
+                       double* classic_cost_out) {
+  if (units <= 0 || num_kv_tiles <= 0 || slots <= 0) return ATTN_ERR_INVALID_ARG;
+  const SplitPlan cl = plan_split(units, num_kv_tiles, slots, 0);
+  const SplitPlan pp = plan_persistent(units, num_kv_tiles, slots);
+  const double cp = persistent_cost(units, num_kv_tiles, pp.ctas);
+  const double cc = classic_cost(cl, num_kv_tiles, slots);
+  if (persistent) *persistent = cp <= cc ? 1 : 0;
+  if (ctas) *ctas = pp.ctas;
+  if (pieces) *pieces = pp.split;
+  if (persistent_cost_out) *persistent_cost_out = cp;
+  if (classic_cost_out) *classic_cost_out = cc;
+  return ATTN_OK;
+}
+
 int attn_plan_split(long long units, int num_kv_tiles, long long slots, int mode, int* split,
                     long long* whole_units, long long* ctas) {
   if (units < 0 || num_kv_tiles < 0 || slots <= 0 || mode < 0 || mode > kMaxSplit)
@@ -310,6 +335,7 @@ int attn_query_split(int B, int H, int S, int D, int dtype, int BM, int BN, int*
   SplitPlan pl;
   LaunchOpts o;
   o.split = g_split_mode.load();
+  o.schedule = g_schedule_mode.load();
   o.plan_out = &pl;
   o.plan_only = true;
   const int rc = dispatch(nullptr, nullptr, nullptr, nullptr, B, H, S, D, S, S, dtype, BM, BN,

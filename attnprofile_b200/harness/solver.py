@@ -44,7 +44,7 @@ def smem_bytes(BM: int, BN: int, HD: int, stages: int) -> int:
     exp_bound = nq == 2 and HD == 64 and nq * (2 * BN + HD) <= TMEM_COLS
     phalves = 2 if (BN >= 64 and not exp_bound) else 1
     off_bar = nq * 128 * HD * 2 + stages * BN * HD * 2
-    num_bars = nq + 2 * stages + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1
+    num_bars = nq + 2 * stages + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1 + nq
     off_misc = off_bar + ((num_bars * 8 + 15) // 16) * 16
     return off_misc + 16 + 1024
 
@@ -59,7 +59,7 @@ def lib_stages(BM: int, BN: int, HD: int, cap: int = 8) -> int:
     nsbuf = 2 if nq * (2 * BN + HD) <= TMEM_COLS else 1
     exp_bound = nq == 2 and HD == 64 and nq * (2 * BN + HD) <= TMEM_COLS
     phalves = 2 if (BN >= 64 and not exp_bound) else 1
-    bars2 = nq + 2 * 2 + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1
+    bars2 = nq + 2 * 2 + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1 + nq
     off_kv = nq * 128 * HD * 2
     best = 0
     for s in range(2, cap + 1):

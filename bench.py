@@ -71,6 +71,8 @@ def parse():
                          "point-to-point and report its time separately")
     ap.add_argument("--preroll-s", type=float, default=0.5,
                     help="untimed back-to-back launches before timing (clock warm-up)")
+    ap.add_argument("--schedule", type=int, default=0, choices=[0, 1, 2],
+                    help="attn_set_schedule mode: 0 automatic (default), 1 classic, 2 persistent")
     ap.add_argument("--no-sub", action="store_true",
                     help="skip the sub-records (C4/C5 strong scaling at every N, C3 at N=1)")
     a = ap.parse_args()
@@ -416,6 +418,7 @@ def main():
 
     ctx = Ctx()
     n, rank, dev = ctx.world, ctx.rank, ctx.dev
+    ap.set_schedule(args.schedule)
     w = WORKLOADS[args.workload]
     cfg = config_of(args.workload, args, n)
     m = measure(ctx, args.workload, args.bm, args.bn, args.steps, args.warmup, args.preroll_s,
@@ -553,6 +556,8 @@ def main():
                          "kernel": "attn_fwd_kernel"},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
+            "schedule": ap.query_split(cfg["B"], w["H"], S, D, BM=args.bm, BN=args.bn,
+                                       dtype=0 if w["dtype"] == "f16" else 1),
         }
         line.update(subs)
         if gather is not None:

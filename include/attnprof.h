@@ -154,6 +154,35 @@ int attn_query_config(int D, int BM, int BN, int dtype, int* num_threads, int* s
  * (tuning/attn_test.cu:1583-1663).
  */
 int attn_set_split(int mode);
+
+/*
+ * Schedule of the launch (two-tile variants with one S buffer per tile:
+ * BM = 256 with BN = 96 or 128 at D = 128, BN = 128 at D = 64).
+ *   classic     one CTA per unit of BM query rows (or per key range of a
+ *               unit of the last wave, attn_set_split); a grid of units.
+ *   persistent  one resident CTA per SM slot, each running an equal share of
+ *               the launch's (unit, key tile) steps in order, crossing unit
+ *               boundaries: the next unit's Q and first S overlap the
+ *               current unit's end, and no wave is left partly empty.  A
+ *               unit cut between two CTAs is finished by the CTA holding its
+ *               first key tile, which adds the other pieces' partial results
+ *               (written by the next CTAs first) in key order.  Launched
+ *               cooperatively (all CTAs resident at once).
+ * attn_set_schedule -- mode 0 automatic (persistent where the variant has it
+ *   and its cost model is no slower; only with the automatic split mode),
+ *   1 classic only, 2 persistent whenever the variant has it.
+ * attn_plan_schedule -- the host planner alone (no GPU): whether the
+ *   automatic mode picks the persistent schedule for U units of
+ *   num_kv_tiles key tiles on `slots` resident CTAs, its grid, the most
+ *   pieces a unit is cut into, and both schedules' modelled costs (in
+ *   key-tile periods of one CTA).
+ * No counterpart in the reference, whose grid is one CTA per unit
+ * (tuning/attn_test.cu:1583-1663).
+ */
+int attn_set_schedule(int mode);
+int attn_plan_schedule(long long units, int num_kv_tiles, long long slots, int* persistent,
+                       long long* ctas, int* pieces, double* persistent_cost,
+                       double* classic_cost);
 int attn_plan_split(long long units, int num_kv_tiles, long long slots, int mode, int* split,
                     long long* whole_units, long long* ctas);
 int attn_query_split(int B, int H, int S, int D, int dtype, int BM, int BN, int* split,
