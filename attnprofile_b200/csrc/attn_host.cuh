@@ -62,10 +62,11 @@ struct SplitPlan {
   long long units = 0, whole = 0, ctas = 0;
   size_t ws_bytes = 0;           // workspace for the split units (0: none)
   size_t off_ml = 0, off_cnt = 0, cnt_bytes = 0;
-  // Persistent schedule: `ctas` resident CTAs share total_steps (unit, key
-  // tile) steps evenly; split = the most pieces any unit is cut into.
+  // Persistent schedule: `ctas` resident CTAs, rr_rounds whole units each
+  // round-robin, then total_steps tail steps (from step tail_base) shared
+  // evenly; split = the most pieces any unit is cut into.
   bool persistent = false;
-  long long total_steps = 0;
+  long long rr_rounds = 0, tail_base = 0, total_steps = 0;
 };
 
 struct LaunchOpts {
@@ -127,23 +128,32 @@ inline SplitPlan plan_split(long long units, int n_kv, long long slots, int mode
   return pl;
 }
 
-// Persistent schedule (variants with AttnConfig::PERSIST_OK): `grid`
-// resident CTAs, CTA c running steps [c T / grid, (c + 1) T / grid) of the
-// T = units * n_kv (unit, key tile) steps.  Cost model in key-tile periods of
-// one CTA: its steps, plus a fixed 2 (its first Q load and pipeline fill,
-// its last epilogue), plus 0.5 per item boundary inside its range (the
-// next item's first S is computed under the epilogue), plus for a range
-// that starts or ends inside a unit 1 (partial write) and 1.5 + 0.5 per
-// further piece (merge).  The grid size that minimises the model wins; the
-// classic plan (plan_split) is costed by its own model, and the persistent
-// schedule is taken when it is no slower.
+// Persistent schedule (variants with AttnConfig::PERSIST_OK) on `grid`
+// resident CTAs: with R = units / grid and r = units % grid, every CTA first
+// runs R' whole units round-robin (R' = R when r = 0, else R - 1, at least 0),
+// then an equal share of the remaining units' steps (the tail: the last
+// r + grid units, or all of them when R = 0), so each share spans at least a
+// unit whenever the units outnumber the CTAs.  Cost model in key-tile periods
+// of one CTA: its steps, plus a fixed 2 (its first Q load and pipeline fill,
+// its last epilogue), plus 0.5 per item boundary (the next item's first S is
+// computed under the epilogue), plus, when its tail share starts or ends
+// inside a unit, 1 (partial write) and 1.5 + 0.5 per further piece (merge).
+// The grid size with the lowest cost wins; the classic plan (plan_split) is
+// costed by its own model, and the persistent schedule is taken when it is
+// no slower.
+inline long long rr_rounds_of(long long units, long long grid) {
+  const long long R = units / grid, r = units % grid;
+  return r == 0 ? R : (R > 0 ? R - 1 : 0);
+}
+
 inline double persistent_cost(long long units, int n_kv, long long grid) {
-  const long long T = units * n_kv;
-  const long long steps = (T + grid - 1) / grid;
-  const long long items = (steps + n_kv - 1) / n_kv + 1;
-  double c = static_cast<double>(steps) + 2.0 + 0.5 * static_cast<double>(items - 1);
-  if (T % grid != 0 || (T / grid) % n_kv != 0) {
-    const long long pieces = std::min<long long>((n_kv + steps - 1) / steps + 1, 64);
+  const long long rr = rr_rounds_of(units, grid);
+  const long long Tt = (units - rr * grid) * n_kv;  // tail steps
+  const long long share = (Tt + grid - 1) / grid;
+  const long long items = rr + (share + n_kv - 1) / n_kv + 1;
+  double c = static_cast<double>(rr * n_kv + share) + 2.0 + 0.5 * static_cast<double>(items - 1);
+  if (Tt % grid != 0 || (Tt / grid) % n_kv != 0) {
+    const long long pieces = std::min<long long>((n_kv + share - 1) / share + 1, 64);
     c += 1.0 + 1.5 + 0.5 * static_cast<double>(pieces - 1);
   }
   return c;
@@ -162,13 +172,13 @@ inline double classic_cost(const SplitPlan& pl, int n_kv, long long slots) {
 }
 
 // The persistent plan for `units` units of n_kv key tiles on `slots`
-// resident CTAs: the grid size with the lowest modelled cost (grid <= T).
+// resident CTAs: the grid size with the lowest modelled cost (grid <= the
+// tail's steps).
 inline SplitPlan plan_persistent(long long units, int n_kv, long long slots) {
   SplitPlan pl;
   pl.persistent = true;
   pl.units = units;
-  pl.total_steps = units * n_kv;
-  const long long gmax = std::min<long long>(slots, pl.total_steps);
+  const long long gmax = std::min<long long>(slots, units * n_kv);
   long long best_g = gmax;
   double best = persistent_cost(units, n_kv, gmax);
   for (long long g = gmax - 1; g >= 1 && g >= gmax / 2; --g) {
@@ -179,18 +189,23 @@ inline SplitPlan plan_persistent(long long units, int n_kv, long long slots) {
     }
   }
   pl.ctas = best_g;
+  pl.rr_rounds = rr_rounds_of(units, best_g);
+  pl.tail_base = pl.rr_rounds * best_g * n_kv;
+  pl.total_steps = (units - pl.rr_rounds * best_g) * n_kv;  // tail steps
   // Units cut between CTAs, and the most pieces any of them has.
   long long cut_units = 0;
   int most = 1;
+  const long long Tt = pl.total_steps;
+  const int g = static_cast<int>(best_g);
   for (long long u0 = -1, c = 1; c < best_g; ++c) {
-    const long long b = c * pl.total_steps / best_g;
+    const long long b = pl.tail_base + c * Tt / best_g;
     if (b % n_kv == 0) continue;
     const long long u = b / n_kv;
     if (u != u0) {
       ++cut_units;
       u0 = u;
-      const long long first = step_owner(u * n_kv, pl.total_steps, static_cast<int>(best_g));
-      const long long last = step_owner((u + 1) * n_kv - 1, pl.total_steps, static_cast<int>(best_g));
+      const long long first = step_owner(u * n_kv - pl.tail_base, Tt, g);
+      const long long last = step_owner((u + 1) * n_kv - 1 - pl.tail_base, Tt, g);
       most = std::max<int>(most, static_cast<int>(last - first + 1));
     }
   }
@@ -411,7 +426,7 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   // automatic mode when its model is no slower than the classic plan's.
   // (A CTA's steps are counted in 32 bits.)
   if (C::PERSIST_OK && o.split == 0 && o.schedule != 1 && BH * qt > 0 &&
-      BH * qt * n_kv / slots < (1ll << 30)) {
+      BH * qt * n_kv / slots < (1ll << 29)) {
     SplitPlan pp = plan_persistent(BH * qt, n_kv, slots);
     if (o.schedule == 2 ||
         persistent_cost(BH * qt, n_kv, pp.ctas) <= classic_cost(plan, n_kv, slots)) {
@@ -448,7 +463,8 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   p.prof = o.prof;
   p.prof_cta = o.prof_cta;
   p.grid = static_cast<int>(plan.ctas);
-  p.total_steps = plan.total_steps;
+  p.tail_steps = plan.total_steps;
+  if (plan.persistent) p.num_whole = static_cast<int>(plan.rr_rounds);
   p.o_ptr = O;
   p.o_head_elems = q_rows * D;
 

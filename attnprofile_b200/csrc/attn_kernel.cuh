@@ -106,7 +106,7 @@ struct AttnParams {
   // (1 < split <= kMaxSplit, split <= num_kv_tiles), one CTA each, merged by
   // whichever of them finishes last.  No split: num_whole = all units.
   int qt_per_bh;
-  int num_whole;
+  int num_whole;               // persistent schedule: round-robin rounds of whole units
   int split;
   float4* ws_o;                // [split units][split][D / 4][BM] (float4 columns of partial O)
   float2* ws_ml;               // [split units][split][BM]: (row max in raw score units, row sum)
@@ -118,14 +118,16 @@ struct AttnParams {
   unsigned long long* prof;    // PROFILE builds: stamp buffer, may be null
   int prof_cta;                // linear CTA index to profile
   // Persistent schedule (the kernel's PERSIST variant): the grid is `grid`
-  // CTAs that are all resident at once; CTA c runs steps
-  // [c * total_steps / grid, (c + 1) * total_steps / grid) of the sequence
-  // of (unit, key tile) steps, unit-major, as a series of items
-  // (ItemCursor).  Its workspace: ws_o / ws_ml hold one partial block per
-  // CTA, ws_cnt one counter per (CTA, Q tile).  O is stored from registers
-  // straight to o_ptr.
+  // CTAs that are all resident at once.  CTA c first runs the whole units
+  // c, c + grid, ... (num_whole of them, "rounds"), then the tail: steps
+  // [base + c * tail_steps / grid, base + (c + 1) * tail_steps / grid),
+  // base = num_whole * grid * num_kv_tiles, of the sequence of (unit, key
+  // tile) steps, unit-major (ItemCursor).  Its workspace: ws_o / ws_ml hold
+  // one partial block per CTA, ws_cnt one counter per (CTA, Q tile).  O is
+  // stored from registers straight to o_ptr.  (The parameter block keeps
+  // its size: the classic kernels' register allocation is sensitive to it.)
   int grid;
-  long long total_steps;
+  long long tail_steps;
   void* o_ptr;
   long long o_head_elems;      // elements from one (batch, head) block of O to the next
 };
@@ -142,16 +144,22 @@ struct WorkTile {
 };
 
 // ---------------------------------------------------------------------------
-// Persistent schedule: items of a CTA's step range
+// Persistent schedule: items of a CTA
 // ---------------------------------------------------------------------------
-// The steps of a launch are (unit u, key tile k) in the order u * num_kv_tiles
-// + k; CTA c owns [floor(c T / G), floor((c + 1) T / G)), T = total steps,
-// G = grid <= T.  Its range cut at unit boundaries gives its items: at most
-// one at each end covers only part of a unit.  A unit cut between CTAs is
-// finished by the piece holding its first key tile (kMerger), which is the
-// last item of its CTA c0; every other piece (kWriter) is the first item of
-// one of the CTAs c0 + 1 .. c1, writes its partial result into that CTA's
-// workspace slot and counts in on c0's counter.
+// The steps of a launch are (unit u, key tile k), numbered u * num_kv_tiles
+// + k.  CTA c of G first runs the whole units c, c + G, ..., c + (R - 1) G
+// (R = rr_rounds; the units running at any one time are neighbours, so the
+// K/V of their heads stay in L2), then its share of the tail -- the steps of
+// the remaining units, T_t of them from step tail_base -- namely
+// [tail_base + floor(c T_t / G), tail_base + floor((c + 1) T_t / G)).  The
+// host makes the tail at least G units long, so each share spans a unit or
+// more and a unit is cut at most once.  A share cut at unit boundaries gives
+// the CTA's tail items; a unit cut between two CTAs is finished by the piece
+// holding its first key tile (kMerger), the last item of its CTA c0; the
+// other piece (kWriter) is the first tail item of CTA c0 + 1, which writes
+// its partial result into that CTA's workspace slot and counts in on c0's
+// counter.  (The code allows any number of pieces: writers are the first
+// tail items of CTAs c0 + 1 .. c1.)
 enum : int { kWhole = 0, kMerger = 1, kWriter = 2 };
 
 struct Item {
@@ -159,19 +167,39 @@ struct Item {
   int peer;  // kMerger: last CTA holding a piece of the unit; kWriter: the merging CTA
 };
 
-// The CTA whose range holds global step x: the largest c with
-// floor(c T / G) <= x.
+// The CTA whose tail share holds tail step x (counted from tail_base): the
+// largest c with floor(c T / G) <= x.
 __host__ __device__ __forceinline__ int step_owner(long long x, long long T, int G) {
   return static_cast<int>(((x + 1) * G - 1) / T);
 }
 
+__device__ __forceinline__ long long tail_base_of(const AttnParams& p) {
+  return static_cast<long long>(p.num_whole) * p.grid * p.num_kv_tiles;
+}
+
 struct ItemCursor {
+  int cta, rr, rr_end;
   long long cur, end;
-  __device__ __forceinline__ void init(int cta, const AttnParams& p) {
-    cur = static_cast<long long>(cta) * p.total_steps / p.grid;
-    end = static_cast<long long>(cta + 1) * p.total_steps / p.grid;
+  __device__ __forceinline__ void init(int c, const AttnParams& p) {
+    cta = c;
+    rr = 0;
+    rr_end = p.num_whole;
+    const long long base = tail_base_of(p);
+    cur = base + static_cast<long long>(c) * p.tail_steps / p.grid;
+    end = base + static_cast<long long>(c + 1) * p.tail_steps / p.grid;
   }
   __device__ __forceinline__ bool next(Item& it, const AttnParams& p, int BM) {
+    if (rr < rr_end) {
+      const long long u = static_cast<long long>(rr) * p.grid + cta;
+      it.bh = static_cast<int>(u / p.qt_per_bh);
+      it.q_row0 = static_cast<int>(u % p.qt_per_bh) * BM;
+      it.kv_lo = 0;
+      it.n = p.num_kv_tiles;
+      it.role = kWhole;
+      it.peer = -1;
+      ++rr;
+      return true;
+    }
     if (cur >= end) return false;
     const long long nkv = p.num_kv_tiles;
     const long long u = cur / nkv;
@@ -186,10 +214,10 @@ struct ItemCursor {
       it.peer = -1;
     } else if (lo == 0) {
       it.role = kMerger;
-      it.peer = step_owner((u + 1) * nkv - 1, p.total_steps, p.grid);
+      it.peer = step_owner((u + 1) * nkv - 1 - tail_base_of(p), p.tail_steps, p.grid);
     } else {
       it.role = kWriter;
-      it.peer = step_owner(u * nkv, p.total_steps, p.grid);
+      it.peer = step_owner(u * nkv - tail_base_of(p), p.tail_steps, p.grid);
     }
     cur += it.n;
     return true;
@@ -1302,8 +1330,8 @@ __device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* 
   load_q(it);
   if (p.fault_mode == 1) return;  // test hook: K/V never arrive; consumers time out
 
-  long long t = 0;  // ring item counter: K_J is item 2J, V_J item 2J + 1
-  long long last_issued[C::STAGES];
+  int t = 0;  // ring item counter: K_J is item 2J, V_J item 2J + 1
+  int last_issued[C::STAGES];
 #pragma unroll
   for (int s = 0; s < C::STAGES; ++s) last_issued[s] = -1;
   bool ok = true;
@@ -1311,25 +1339,24 @@ __device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* 
   // k_bar >= 0: the K load completes on that slot's FULL barrier (armed by
   // the V item just before it for both tiles' bytes); its own gets a plain
   // arrival to keep its phase count.
-  auto produce = [&](bool is_k, const Item& x, int j, long long J, bool joint, int k_bar) {
-    const int s = static_cast<int>(t % C::STAGES);
+  auto produce = [&](bool is_k, const Item& x, int j, int J, bool joint, int k_bar) {
+    const int s = t % C::STAGES;
     if (t >= C::STAGES) {
       uint32_t eb, par;
       if constexpr (C::V_RELEASE_WITH_K) {
-        const long long m = (t - C::STAGES + 1) / 2;  // the K item whose commit frees slot s
-        eb = bar(C::BAR_KV_EMPTY + static_cast<int>((2 * m) % C::STAGES));
-        par = static_cast<uint32_t>((m / C::K_SLOT_PERIOD) & 1);
+        const int m = (t - C::STAGES + 1) / 2;  // the K item whose commit frees slot s
+        eb = bar(C::BAR_KV_EMPTY + (2 * m) % C::STAGES);
+        par = static_cast<uint32_t>(m / C::K_SLOT_PERIOD) & 1u;
       } else {
         eb = bar(C::BAR_KV_EMPTY + s);
-        par = static_cast<uint32_t>((t / C::STAGES - 1) & 1);
+        par = static_cast<uint32_t>(t / C::STAGES - 1) & 1u;
       }
       if (!wait_bar(eb, par, w, kSiteKvEmpty)) {
         ok = false;
         return;
       }
     }
-    const int sl = J < kProfSlots ? static_cast<int>(J) : kProfSlots;
-    prof.stamp(is_k ? kPhLoadK : kPhLoadV, sl, 0);
+    prof.stamp(is_k ? kPhLoadK : kPhLoadV, J < kProfSlots ? J : kProfSlots, 0);
     uint32_t full = bar(C::BAR_KV_FULL + s);
     if (k_bar >= 0) {
       ptx::mbar_arrive(full);
@@ -1353,7 +1380,7 @@ __device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* 
   };
 
   produce(true, it, 0, 0, false, -1);
-  long long J = 0;
+  int J = 0;
   int item = 0;
   while (ok) {
     for (int j = 0; j < it.n && ok; ++j, ++J) {
@@ -1361,7 +1388,7 @@ __device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* 
       // V_J and K_{J+1} land together only inside an item: at an item's end
       // the next K waits for Q_FREE, and V_J must not wait for it.
       const bool joint = C::KV_JOINT_FULL && !last;
-      const int sv = static_cast<int>(t % C::STAGES);
+      const int sv = t % C::STAGES;
       produce(false, it, j, J, joint, -1);
       if (!ok) break;
       if (!last) {
@@ -1392,7 +1419,7 @@ __device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* 
 #pragma unroll
     for (int s = 0; s < C::STAGES; ++s) {
       if (last_issued[s] < 0) continue;
-      const uint32_t r = static_cast<uint32_t>((last_issued[s] / C::STAGES) & 1);
+      const uint32_t r = static_cast<uint32_t>(last_issued[s] / C::STAGES) & 1u;
       while (!ptx::mbar_try_wait(bar(C::BAR_KV_FULL + s), r)) {
         if (ptx::globaltimer_ns() - t0 > w.timeout_ns) break;
       }
@@ -1419,12 +1446,21 @@ __device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnPar
   bool has_nx = cur.next(nx, p, C::BM);
   bool ok = true;
 
-  long long t = 0;
+  // Ring position of the next item: slot and phase parity, advanced
+  // incrementally (no division on the issuing thread, which sits on the
+  // per-tile chain).
+  int rs = 0;
+  uint32_t rph = 0;
+  auto ring_advance = [&]() {
+    if (++rs == C::STAGES) {
+      rs = 0;
+      rph ^= 1u;
+    }
+  };
   auto ring_wait = [&](int& stage) -> bool {
-    stage = static_cast<int>(t % C::STAGES);
-    const bool r = wait_bar(bar(C::BAR_KV_FULL + stage),
-                            static_cast<uint32_t>((t / C::STAGES) & 1), w, kSiteKvFull);
-    ++t;
+    stage = rs;
+    const bool r = wait_bar(bar(C::BAR_KV_FULL + stage), rph, w, kSiteKvFull);
+    ring_advance();
     if (r) ptx::tc_fence_after();
     return r;
   };
@@ -1483,13 +1519,13 @@ __device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnPar
 
   constexpr int KSTEPS = C::BN / 16;
   constexpr int KSPLIT = C::PHALVES == 2 ? 2 * C::PSPLIT_CHUNKS : KSTEPS;
-  long long J = 0;
+  int J = 0;
   int item = 0;
   while (ok) {
     for (int j = 0; j < it.n && ok; ++j, ++J) {
       const bool last = j == it.n - 1;
       const bool more = !last || has_nx;  // is there a step J + 1 in this CTA?
-      const int sl = J < kProfSlots ? static_cast<int>(J) : kProfSlots;
+      const int sl = J < kProfSlots ? J : kProfSlots;
       int sv;
       prof.stamp(kPhVWait, sl, 0);
       if (!(ok = ring_wait(sv))) break;  // V_J (and K_{J+1} when it landed with it)
@@ -1502,14 +1538,14 @@ __device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnPar
         for (int h = 0; h < C::PHALVES; ++h) {
           if (h == C::PHALVES - 1 && more && sk < 0) {
             if (C::KV_JOINT_FULL && !last) {
-              sk = static_cast<int>(t % C::STAGES);  // landed with V_J
-              ++t;
+              sk = rs;  // landed with V_J
+              ring_advance();
             } else if (!(ok = ring_wait(sk))) {
               break;
             }
-            if (J + 1 < kProfSlots) prof.stamp(kPhLoadK, static_cast<int>(J + 1), 1);
+            if (J + 1 < kProfSlots) prof.stamp(kPhLoadK, J + 1, 1);
           }
-          if (!(ok = wait_bar(bar(pb + h), static_cast<uint32_t>(J & 1), w, kSitePReady))) break;
+          if (!(ok = wait_bar(bar(pb + h), static_cast<uint32_t>(J) & 1u, w, kSitePReady))) break;
           ptx::tc_fence_after();
           if (h == 0) {
             if (i == 0) prof.stamp(kPhPV, sl, 0);
@@ -1530,7 +1566,7 @@ __device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnPar
               break;
             ptx::tc_fence_after();
           }
-          if (i == 0 && J + 1 < kProfSlots) prof.stamp(kPhQK, static_cast<int>(J + 1), 0);
+          if (i == 0 && J + 1 < kProfSlots) prof.stamp(kPhQK, J + 1, 0);
           issue_s(i, sk);
           signal(bar(C::BAR_S_FULL + i));
           if (nj == ni.n - 1) signal(bar(C::BAR_Q_FREE + i));  // the item's last S has read Q_i

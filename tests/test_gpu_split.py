@@ -18,8 +18,12 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(autouse=True)
 def _restore_split(engine):
+    # These tests are about the classic schedule's key split; the persistent
+    # schedule (tests/test_gpu_persistent.py) has its own plan.
+    engine.set_schedule(1)
     yield
     engine.set_split(0)
+    engine.set_schedule(0)
 
 
 def run_mode(engine, q, k, v, BM, BN, mode):

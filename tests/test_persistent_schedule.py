@@ -2,13 +2,16 @@
 (attnprofile_b200/csrc/attn_kernel.cuh: ItemCursor, step_owner,
 load_role_persistent, mma_role_persistent, softmax_role_persistent).
 
-1. Items: CTA c of G owns steps [c T / G, (c + 1) T / G) of the T = U * n_kv
-   (unit, key tile) steps.  Over every CTA the items cover each step once, in
-   order; a unit cut between CTAs has exactly one kMerger piece (its first key
-   tile, the last item of its CTA c0, peer = the last CTA c1 holding a piece)
-   and its other pieces are kWriter items, the first items of CTAs
-   c0 + 1 .. c1, each naming c0.  The host planner's grid and most pieces per
-   unit (attn_plan_schedule) agree with this model.
+1. Items: CTA c of G first runs the whole units c, c + G, ... (R' rounds:
+   R' = U // G when G divides U, else max(U // G - 1, 0)), then its share
+   [base + c T_t / G, base + (c + 1) T_t / G) of the remaining T_t steps
+   (base = R' G n_kv).  Over every CTA the items cover each step once; a
+   unit cut between CTAs has exactly one kMerger piece (its first key tile,
+   the last item of its CTA c0, peer = the last CTA c1 holding a piece) and
+   its other pieces are kWriter items, the first tail items of CTAs
+   c0 + 1 .. c1, each naming c0; with U >= G every unit has at most two
+   pieces.  The host planner's grid and most pieces per unit
+   (attn_plan_schedule) agree with this model.
 2. Barrier protocol: a discrete-event model of one CTA -- the producer, the
    TMA engine, the MMA issuer, the tensor pipe (in order; a commit arrives
    once every earlier MMA has executed) and the two softmax warpgroups --
@@ -32,20 +35,27 @@ def step_owner(x, T, G):
     return ((x + 1) * G - 1) // T
 
 
+def rr_rounds(U, G):
+    R, r = divmod(U, G)
+    return R if r == 0 else max(R - 1, 0)
+
+
 def items_of(c, U, nkv, G):
-    T = U * nkv
-    cur, end = c * T // G, (c + 1) * T // G
-    out = []
+    rr = rr_rounds(U, G)
+    out = [dict(u=k * G + c, lo=0, n=nkv, role="whole", peer=-1, tail=False) for k in range(rr)]
+    base = rr * G * nkv
+    Tt = (U - rr * G) * nkv
+    cur, end = base + c * Tt // G, base + (c + 1) * Tt // G
     while cur < end:
         u, lo = divmod(cur, nkv)
         hi = min(nkv, lo + (end - cur))
         if lo == 0 and hi == nkv:
             role, peer = "whole", -1
         elif lo == 0:
-            role, peer = "merger", step_owner((u + 1) * nkv - 1, T, G)
+            role, peer = "merger", step_owner((u + 1) * nkv - 1 - base, Tt, G)
         else:
-            role, peer = "writer", step_owner(u * nkv, T, G)
-        out.append(dict(u=u, lo=lo, n=hi - lo, role=role, peer=peer))
+            role, peer = "writer", step_owner(u * nkv - base, Tt, G)
+        out.append(dict(u=u, lo=lo, n=hi - lo, role=role, peer=peer, tail=True))
         cur += hi - lo
     return out
 
@@ -66,23 +76,32 @@ def test_items_cover_every_step_once_with_one_merger_per_cut_unit(U, nkv, G):
         for k, it in enumerate(its):
             seen += [it["u"] * nkv + it["lo"] + j for j in range(it["n"])]
             pieces.setdefault(it["u"], []).append((c, k, len(its), it))
-    assert seen == list(range(T))
+    assert sorted(seen) == list(range(T))
     for u, ps in pieces.items():
+        ps.sort(key=lambda p: p[3]["lo"])
         if len(ps) == 1:
             assert ps[0][3]["role"] == "whole"
             continue
+        if U >= G:
+            assert len(ps) == 2, "a unit is cut at most once when units >= CTAs"
         c0, k0, nk0, m = ps[0]
         assert m["role"] == "merger" and m["lo"] == 0 and k0 == nk0 - 1
         assert m["peer"] == ps[-1][0]
         assert [p[0] for p in ps] == list(range(c0, m["peer"] + 1))
         for c, k, nk, it in ps[1:]:
-            assert it["role"] == "writer" and k == 0 and it["peer"] == c0
-    # one writer slot per CTA (its first item), one counter per merging CTA
+            first_tail = min(i for i, x in enumerate(items_of(c, U, nkv, G)) if x["tail"])
+            assert it["role"] == "writer" and k == first_tail and it["peer"] == c0
+    # one writer slot per CTA (its first tail item), one counter per merging CTA
     for c in range(G):
         its = items_of(c, U, nkv, G)
         assert sum(it["role"] == "writer" for it in its) <= 1
         assert sum(it["role"] == "merger" for it in its) <= 1
-        assert all(it["role"] != "writer" for it in its[1:])
+        assert all(x["tail"] for x in its[rr_rounds(U, G):])
+    # the whole units that run round-robin are neighbours at every moment
+    rr = rr_rounds(U, G)
+    for k in range(rr):
+        assert sorted(items_of(c, U, nkv, G)[k]["u"] for c in range(G)) == \
+            list(range(k * G, (k + 1) * G))
 
 
 @pytest.mark.parametrize("U,nkv,slots", [(256, 32, 148), (8192, 64, 148), (64, 64, 148),
@@ -91,13 +110,11 @@ def test_host_planner_matches_the_model(engine, U, nkv, slots):
     plan = engine.plan_schedule(U, nkv, slots)
     G = plan["ctas"]
     assert 1 <= G <= min(slots, U * nkv)
-    most = 1
     per_unit = {}
     for c in range(G):
         for it in items_of(c, U, nkv, G):
             per_unit[it["u"]] = per_unit.get(it["u"], 0) + 1
-    most = max(per_unit.values())
-    assert plan["pieces"] == most
+    assert plan["pieces"] == max(per_unit.values())
     # the benchmark shapes take the persistent schedule
     if (U, nkv, slots) in ((256, 32, 148), (8192, 64, 148)):
         assert plan["persistent"] and plan["persistent_cost"] < plan["classic_cost"]
@@ -359,7 +376,8 @@ class Sim:
 
 @pytest.mark.parametrize("stages", [2, 3, 4, 5, 6, 8])
 @pytest.mark.parametrize("U,nkv,G,cta", [(256, 32, 148, 0), (256, 32, 148, 1), (256, 32, 148, 147),
-                                         (5, 3, 2, 1), (7, 1, 3, 2), (4, 6, 3, 1), (2, 5, 1, 0)])
+                                         (5, 3, 2, 1), (7, 1, 3, 2), (4, 6, 3, 1), (2, 5, 1, 0),
+                                         (40, 4, 9, 3), (41, 3, 8, 7)])
 def test_barrier_protocol_under_random_interleavings(stages, U, nkv, G, cta):
     its = items_of(cta, U, nkv, G)
     for seed in range(12):
