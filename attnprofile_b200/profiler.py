@@ -137,7 +137,10 @@ def run(B=1, H=16, S=4096, D=128, BM=256, BN=128, dtype="f16", runs=20, cta=None
     g = torch.Generator(device="cuda").manual_seed(seed)
     Q, K, V = (torch.randn(B, H, S, D, generator=g, device="cuda").to(dt) for _ in range(3))
     n_qt = (S + BM - 1) // BM
-    cta = (n_qt * B * H) // 2 if cta is None else cta  # a CTA from the middle of the grid
+    # a CTA from the middle of the grid (the persistent schedule's grid is
+    # one CTA per resident slot, not one per unit)
+    ctas = ap.query_split(B, H, S, D, BM=BM, BN=BN, dtype=0 if dtype == "f16" else 1)["ctas"]
+    cta = min(n_qt * B * H, ctas) // 2 if cta is None else cta
     for _ in range(3):
         ap.attn(Q, K, V, BM=BM, BN=BN)
     stamps = []
@@ -149,6 +152,22 @@ def run(B=1, H=16, S=4096, D=128, BM=256, BN=128, dtype="f16", runs=20, cta=None
     if rc != 0:
         raise RuntimeError(f"device status {site:#x}")
     return stamps if raw else summarize(stamps)
+
+
+def step_starts(st) -> str:
+    """Cycles between consecutive SOFTMAX starts of tile 0, per step of the
+    profiled CTA (its first 32 steps, across its items): a long gap marks an
+    item boundary of the persistent schedule."""
+    import numpy as np
+    a = np.asarray(st, dtype=np.int64)
+    sb = a[PHASES.index("SOFTMAX"), :, 0]
+    rows = ["| step | SOFTMAX start | since previous |", "|---|---|---|"]
+    for j in range(sb.shape[0]):
+        if sb[j] == 0:
+            continue
+        d = "-" if j == 0 or sb[j - 1] == 0 else f"{int(sb[j] - sb[j - 1])}"
+        rows.append(f"| {j} | {int(sb[j] - sb[0])} | {d} |")
+    return "\n".join(rows)
 
 
 def table_header() -> str:
@@ -172,14 +191,24 @@ def main(argv=None):
     ap_.add_argument("--runs", type=int, default=20)
     ap_.add_argument("--timeline", type=int, default=0, metavar="N",
                      help="also print N iterations (from 8) of one run's event timeline per tile")
+    ap_.add_argument("--schedule", type=int, default=0, choices=[0, 1, 2],
+                     help="attn_set_schedule mode (0 automatic, 1 classic, 2 persistent)")
+    ap_.add_argument("--cta", type=int, default=None, help="CTA to profile (default: middle)")
+    ap_.add_argument("--steps", action="store_true",
+                     help="also print the per-step SOFTMAX starts of one run (item boundaries)")
     a = ap_.parse_args(argv)
+    import attnprofile_b200 as ap
+    ap.set_schedule(a.schedule)
     print(f"B={a.b} H={a.h} S={a.s} D={a.d} {a.dtype}: cycles (clock64) per phase, "
           f"mean over KV iterations 0-31 and {a.runs} runs")
     print(table_header())
     for t in a.tiles.split(","):
         bm, bn = (int(x) for x in t.split("x"))
-        st = run(a.b, a.h, a.s, a.d, bm, bn, a.dtype, a.runs, raw=True)
+        st = run(a.b, a.h, a.s, a.d, bm, bn, a.dtype, a.runs, cta=a.cta, raw=True)
         print(table_row(bm, bn, summarize(st)), flush=True)
+        if a.steps:
+            print(f"\n{bm}x{bn} per-step SOFTMAX starts (cycles, last run):\n"
+                  + step_starts(st[-1]) + "\n", flush=True)
         if a.timeline:
             print(f"\n{bm}x{bn} timeline (cycles, last run):\n" + timeline(st[-1], 8, a.timeline)
                   + "\n", flush=True)
