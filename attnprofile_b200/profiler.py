@@ -170,13 +170,16 @@ def step_starts(st) -> str:
     return "\n".join(rows)
 
 
-def table_header() -> str:
+def table_header(epilogue: bool = False) -> str:
     cols = ["BM", "BN"] + PHASES + ["period"] + SUBPHASES + TRACE_PHASES
+    if epilogue:
+        cols += EPILOGUE_STEPS
     return "| " + " | ".join(cols) + " |\n|" + "---|" * len(cols)
 
 
-def table_row(BM, BN, r) -> str:
-    vals = [f"{r[p]:.0f}" for p in PHASES + ["period"] + SUBPHASES + TRACE_PHASES]
+def table_row(BM, BN, r, epilogue: bool = False) -> str:
+    names = PHASES + ["period"] + SUBPHASES + TRACE_PHASES + (EPILOGUE_STEPS if epilogue else [])
+    vals = [f"{r[p]:.0f}" for p in names]
     return f"| {BM} | {BN} | " + " | ".join(vals) + " |"
 
 
@@ -196,16 +199,18 @@ def main(argv=None):
     ap_.add_argument("--cta", type=int, default=None, help="CTA to profile (default: middle)")
     ap_.add_argument("--steps", action="store_true",
                      help="also print the per-step SOFTMAX starts of one run (item boundaries)")
+    ap_.add_argument("--epilogue", action="store_true",
+                     help="add the epilogue steps (of the CTA's first item) to the table")
     a = ap_.parse_args(argv)
     import attnprofile_b200 as ap
     ap.set_schedule(a.schedule)
     print(f"B={a.b} H={a.h} S={a.s} D={a.d} {a.dtype}: cycles (clock64) per phase, "
           f"mean over KV iterations 0-31 and {a.runs} runs")
-    print(table_header())
+    print(table_header(a.epilogue))
     for t in a.tiles.split(","):
         bm, bn = (int(x) for x in t.split("x"))
         st = run(a.b, a.h, a.s, a.d, bm, bn, a.dtype, a.runs, cta=a.cta, raw=True)
-        print(table_row(bm, bn, summarize(st)), flush=True)
+        print(table_row(bm, bn, summarize(st), a.epilogue), flush=True)
         if a.steps:
             print(f"\n{bm}x{bn} per-step SOFTMAX starts (cycles, last run):\n"
                   + step_starts(st[-1]) + "\n", flush=True)
