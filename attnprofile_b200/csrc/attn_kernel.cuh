@@ -1383,10 +1383,20 @@ __device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* 
   int J = 0;
   int item = 0;
   while (ok) {
+    // The next item's Q tiles go to L2 a few steps ahead, so that their load
+    // into shared memory (which has to wait for Q_FREE) is short.
+    const int pf = it.n > 3 ? it.n - 3 : 0;
     for (int j = 0; j < it.n && ok; ++j, ++J) {
       const bool last = j == it.n - 1;
-      // V_J and K_{J+1} land together only inside an item: at an item's end
-      // the next K waits for Q_FREE, and V_J must not wait for it.
+      if (j == pf && has_nx) {
+#pragma unroll
+        for (int i = 0; i < C::NQ; ++i)
+#pragma unroll
+          for (int d = 0; d < C::DBLK; ++d)
+            ptx::tma_prefetch_l2_3d(tmQ, d * 64, nx.q_row0 + i * C::QROWS, nx.bh);
+      }
+      // V_J and K_{J+1} land together only inside an item; at an item's end
+      // the next item's K_0 has its own barrier.
       const bool joint = C::KV_JOINT_FULL && !last;
       const int sv = t % C::STAGES;
       produce(false, it, j, J, joint, -1);
@@ -1394,6 +1404,10 @@ __device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* 
       if (!last) {
         produce(true, it, j + 1, J + 1, false, joint ? sv : -1);
       } else if (has_nx) {
+        // The next item's K_0 first (it needs only a free slot), then its Q
+        // tiles once this item's last S has read the current ones.
+        produce(true, nx, 0, J + 1, false, -1);
+        if (!ok) break;
 #pragma unroll
         for (int i = 0; i < C::NQ; ++i)
           if (ok && !wait_bar(bar(C::BAR_Q_FREE + i), static_cast<uint32_t>(item & 1), w,
@@ -1402,7 +1416,6 @@ __device__ void load_role_persistent(const CUtensorMap* tmQ, const CUtensorMap* 
         if (!ok) break;
         load_q(nx);
         q_item = item + 1;
-        produce(true, nx, 0, J + 1, false, -1);
       }
     }
     if (!ok || !has_nx) break;
@@ -1511,7 +1524,6 @@ __device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnPar
         if (i == 0) prof.stamp(kPhQK, 0, 0);
         issue_s(i, sk);
         signal(bar(C::BAR_S_FULL + i));
-        if (it.n == 1) signal(bar(C::BAR_Q_FREE + i));
       }
       signal(bar(C::BAR_KV_EMPTY + sk));
     }
@@ -1522,23 +1534,25 @@ __device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnPar
   int J = 0;
   int item = 0;
   while (ok) {
-    for (int j = 0; j < it.n && ok; ++j, ++J) {
-      const bool last = j == it.n - 1;
-      const bool more = !last || has_nx;  // is there a step J + 1 in this CTA?
+    const int n = it.n;
+    // Steps 0 .. n - 2: as in the classic issuer (K_{J+1} of the same item,
+    // which landed with V_J under the joint landing).
+    for (int j = 0; j < n - 1 && ok; ++j, ++J) {
       const int sl = J < kProfSlots ? J : kProfSlots;
       int sv;
       prof.stamp(kPhVWait, sl, 0);
-      if (!(ok = ring_wait(sv))) break;  // V_J (and K_{J+1} when it landed with it)
+      if (!(ok = ring_wait(sv))) break;
       prof.stamp(kPhVWait, sl, 1);
       prof.stamp(kPhLoadV, sl, 1);
       int sk = -1;
-      for (int i = 0; i < C::NQ && ok; ++i) {
+#pragma unroll
+      for (int i = 0; i < C::NQ; ++i) {
         const int pb = C::BAR_P_READY + i * C::PHALVES;
 #pragma unroll
         for (int h = 0; h < C::PHALVES; ++h) {
-          if (h == C::PHALVES - 1 && more && sk < 0) {
-            if (C::KV_JOINT_FULL && !last) {
-              sk = rs;  // landed with V_J
+          if (h == C::PHALVES - 1 && sk < 0) {
+            if constexpr (C::KV_JOINT_FULL) {
+              sk = rs;
               ring_advance();
             } else if (!(ok = ring_wait(sk))) {
               break;
@@ -1554,31 +1568,69 @@ __device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnPar
           issue_pv(i, sv, h == 0 ? 0 : KSPLIT, h == 0 ? KSPLIT : KSTEPS, j == 0);
         }
         if (!ok) break;
-        // The item's result is complete once its last P V is: O_FINAL before
-        // the next item's first S, which need not wait for the epilogue.
-        if (last) signal(bar(C::BAR_O_FINAL + i));
-        if (more) {
-          const Item& ni = last ? nx : it;
-          const int nj = last ? 0 : j + 1;
-          if (last) {
-            if (!(ok = wait_bar(bar(C::BAR_Q + i), static_cast<uint32_t>((item + 1) & 1), w,
-                                kSiteQ)))
-              break;
-            ptx::tc_fence_after();
+        if (i == 0 && J + 1 < kProfSlots) prof.stamp(kPhQK, J + 1, 0);
+        issue_s(i, sk);
+        signal(bar(C::BAR_S_FULL + i));
+        if (C::ODONE_PER_STEP) signal(bar(C::BAR_O_DONE + i));
+        prof.stamp(kPhMmaT0 + i, sl, 1);
+      }
+      if (!ok) break;
+      if constexpr (!C::V_RELEASE_WITH_K) signal(bar(C::BAR_KV_EMPTY + sv));
+      signal(bar(C::BAR_KV_EMPTY + sk));  // with V_RELEASE_WITH_K: V_J's slot too
+    }
+    if (!ok) break;
+
+    // The item's last step.  Every S of the item has been issued: Q_FREE
+    // lets the producer load the next item's Q tiles.  Each tile's last P V
+    // and O_FINAL come before anything of the next item, whose K_0 and Q
+    // tiles are waited for only by the next S.
+    {
+      const int sl = J < kProfSlots ? J : kProfSlots;
+#pragma unroll
+      for (int i = 0; i < C::NQ; ++i) signal(bar(C::BAR_Q_FREE + i));
+      int sv;
+      prof.stamp(kPhVWait, sl, 0);
+      if (!(ok = ring_wait(sv))) break;
+      prof.stamp(kPhVWait, sl, 1);
+      prof.stamp(kPhLoadV, sl, 1);
+      int sk = -1;
+#pragma unroll
+      for (int i = 0; i < C::NQ; ++i) {
+        const int pb = C::BAR_P_READY + i * C::PHALVES;
+#pragma unroll
+        for (int h = 0; h < C::PHALVES; ++h) {
+          if (!(ok = wait_bar(bar(pb + h), static_cast<uint32_t>(J) & 1u, w, kSitePReady))) break;
+          ptx::tc_fence_after();
+          if (h == 0) {
+            if (i == 0) prof.stamp(kPhPV, sl, 0);
+            prof.stamp(kPhMmaT0 + i, sl, 0);
           }
+          issue_pv(i, sv, h == 0 ? 0 : KSPLIT, h == 0 ? KSPLIT : KSTEPS, n == 1);
+        }
+        if (!ok) break;
+        signal(bar(C::BAR_O_FINAL + i));
+        if (has_nx) {
+          if (sk < 0) {
+            if (!(ok = ring_wait(sk))) break;  // the next item's K_0
+            if (J + 1 < kProfSlots) prof.stamp(kPhLoadK, J + 1, 1);
+          }
+          if (!(ok = wait_bar(bar(C::BAR_Q + i), static_cast<uint32_t>(item + 1) & 1u, w,
+                              kSiteQ)))
+            break;
+          ptx::tc_fence_after();
           if (i == 0 && J + 1 < kProfSlots) prof.stamp(kPhQK, J + 1, 0);
           issue_s(i, sk);
           signal(bar(C::BAR_S_FULL + i));
-          if (nj == ni.n - 1) signal(bar(C::BAR_Q_FREE + i));  // the item's last S has read Q_i
         }
         if (C::ODONE_PER_STEP) signal(bar(C::BAR_O_DONE + i));
         prof.stamp(kPhMmaT0 + i, sl, 1);
       }
       if (!ok) break;
       if constexpr (!C::V_RELEASE_WITH_K) signal(bar(C::BAR_KV_EMPTY + sv));
-      if (sk >= 0) signal(bar(C::BAR_KV_EMPTY + sk));  // with V_RELEASE_WITH_K: V_J's slot too
+      if (sk >= 0) signal(bar(C::BAR_KV_EMPTY + sk));
+      ++J;
     }
-    if (!ok || !has_nx) break;
+    if (!has_nx) break;
     it = nx;
     ++item;
     has_nx = cur.next(nx, p, C::BM);
@@ -1618,17 +1670,45 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
   const uint32_t nbar = 1 + qi;
   constexpr int BLK = C::BM * C::D / 4;  // float4 per workspace slot
 
-  // Converts 32 values and stores them at dst (16-byte aligned).
-  auto store32 = [&](T* dst, const float* v) {
+  // Stores columns 32c .. 32c + 31 of O for the rows of this thread's group
+  // of four lanes: the four 16-byte chunks of each lane's row are first
+  // transposed across the group (a two-stage butterfly of shuffles), so
+  // that lane b of the group holds chunk 4c + b of each of the group's four
+  // rows and each store instruction writes 64 contiguous bytes of eight rows
+  // instead of 16 bytes of 32.  Rows >= S are not written.  Every lane of
+  // the warp takes part.
+  auto store32t = [&](T* obase, long long row_g0, int c, const float* v) {
+    uint4 x[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      uint4 u;
-      u.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
-      u.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
-      u.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
-      u.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
-      reinterpret_cast<uint4*>(dst)[q] = u;
+      x[q].x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+      x[q].y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+      x[q].z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+      x[q].w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
     }
+    const int b = lane & 3;
+#pragma unroll
+    for (int m = 1; m < 4; m <<= 1) {
+      const bool hi = (b & m) != 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (q & m) continue;
+        const uint4 snd = hi ? x[q] : x[q | m];
+        uint4 r;
+        r.x = __shfl_xor_sync(0xffffffffu, snd.x, m);
+        r.y = __shfl_xor_sync(0xffffffffu, snd.y, m);
+        r.z = __shfl_xor_sync(0xffffffffu, snd.z, m);
+        r.w = __shfl_xor_sync(0xffffffffu, snd.w, m);
+        if (hi)
+          x[q] = r;
+        else
+          x[q | m] = r;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (row_g0 + j < p.S)
+        *reinterpret_cast<uint4*>(obase + (row_g0 + j) * C::D + (4 * c + b) * 8) = x[j];
   };
 
   ItemCursor cur;
@@ -1652,9 +1732,9 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
     if (!go) break;
     ptx::tc_fence_after();
 
-    const long long grow = static_cast<long long>(it.q_row0) + qi * C::QROWS + row;
-    T* orow = static_cast<T*>(p.o_ptr) + it.bh * p.o_head_elems + grow * C::D;
-    const bool store_row = grow < p.S;
+    // O rows of this thread's group of four lanes start at row_g0.
+    T* obase = static_cast<T*>(p.o_ptr) + it.bh * p.o_head_elems;
+    const long long row_g0 = static_cast<long long>(it.q_row0) + qi * C::QROWS + (row & ~3);
 
     if (it.role == kWriter) {
       if (rec && item == 0) prof.stamp(kPhEpilogue, kEpPartial, 0);
@@ -1748,7 +1828,7 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
         }
 #pragma unroll
         for (int e = 0; e < 32; ++e) acc[e] *= inv_tot;
-        if (store_row) store32(orow + c * 32, acc);
+        store32t(obase, row_g0, c, acc);
       }
       if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 1);
     } else {
@@ -1763,7 +1843,7 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
         float v[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]) * inv;
-        if (store_row) store32(orow + c * 32, v);
+        store32t(obase, row_g0, c, v);
       }
       if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 1);
     }

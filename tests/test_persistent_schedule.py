@@ -260,10 +260,10 @@ class Sim:
                 if not last:
                     yield from produce("K", k, j + 1, J + 1, False, sv)
                 elif k + 1 < len(its):
+                    yield from produce("K", k + 1, 0, J + 1, False, None)
                     for i in range(2):
                         yield from self.wait(f"Q_FREE{i}", k & 1, k)
                     load_q(k + 1)
-                    yield from produce("K", k + 1, 0, J + 1, False, None)
                 J += 1
         self.done.add("producer")
 
@@ -299,40 +299,44 @@ class Sim:
         for i in range(2):
             issue_s(i, sk, 0, 0)
             self.commit(f"S_FULL{i}")
-            if its[0]["n"] == 1:
-                self.commit(f"Q_FREE{i}")
         self.commit(f"EMPTY{sk}")
         J = 0
         for k, it in enumerate(its):
             has_nx = k + 1 < len(its)
-            for j in range(it["n"]):
-                last = j == it["n"] - 1
-                more = not last or has_nx
+            n = it["n"]
+            for j in range(n - 1):          # the item's steps but its last
                 sv = yield from ring_wait()
                 sk = -1
                 for i in range(2):
                     for h in range(2):
-                        if h == 1 and more and sk < 0:
-                            if not last:
-                                sk = t % S
-                                t += 1
-                            else:
-                                sk = yield from ring_wait()
+                        if h == 1 and sk < 0:
+                            sk = t % S   # K_{J+1} landed with V_J (joint landing)
+                            t += 1
                         yield from self.wait(f"P{i}{h}", J & 1, J)
                         issue_pv(i, sv, k, j, h)
-                    if last:
-                        self.commit(f"O_FINAL{i}")
-                    if more:
-                        ni, nj = (k + 1, 0) if last else (k, j + 1)
-                        if last:
-                            yield from self.wait(f"Q{i}", (k + 1) & 1, k + 1)
-                        issue_s(i, sk, ni, nj)
-                        self.commit(f"S_FULL{i}")
-                        if nj == its[ni]["n"] - 1:
-                            self.commit(f"Q_FREE{i}")
-                if sk >= 0:
-                    self.commit(f"EMPTY{sk}")
+                    issue_s(i, sk, k, j + 1)
+                    self.commit(f"S_FULL{i}")
+                self.commit(f"EMPTY{sk}")
                 J += 1
+            # the item's last step
+            for i in range(2):
+                self.commit(f"Q_FREE{i}")
+            sv = yield from ring_wait()
+            sk = -1
+            for i in range(2):
+                for h in range(2):
+                    yield from self.wait(f"P{i}{h}", J & 1, J)
+                    issue_pv(i, sv, k, n - 1, h)
+                self.commit(f"O_FINAL{i}")
+                if has_nx:
+                    if sk < 0:
+                        sk = yield from ring_wait()
+                    yield from self.wait(f"Q{i}", (k + 1) & 1, k + 1)
+                    issue_s(i, sk, k + 1, 0)
+                    self.commit(f"S_FULL{i}")
+            if sk >= 0:
+                self.commit(f"EMPTY{sk}")
+            J += 1
         self.commit("DRAIN")
         yield from self.wait("DRAIN", 0, 0)
         self.done.add("mma")
