@@ -1743,13 +1743,14 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
       const float inv = 1.f / l_run;
       float4* dst = p.ws_o + static_cast<long long>(blockIdx.x) * BLK + rrow;
 #pragma unroll 1
-      for (int c = 0; c < C::D / 32; ++c) {
-        uint32_t o[32];
-        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+      for (int c = 0; c < C::D / 32; c += 2) {
+        uint32_t o[64];
+        ptx::tmem_ld32(lane_base + o_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+        ptx::tmem_ld32(lane_base + o_col + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
         ptx::tmem_wait_ld();
         ptx::reg_fence(o);
 #pragma unroll
-        for (int t4 = 0; t4 < 8; ++t4)
+        for (int t4 = 0; t4 < 16; ++t4)
           dst[(c * 8 + t4) * C::BM] = make_float4(
               __uint_as_float(o[4 * t4 + 0]) * inv, __uint_as_float(o[4 * t4 + 1]) * inv,
               __uint_as_float(o[4 * t4 + 2]) * inv, __uint_as_float(o[4 * t4 + 3]) * inv);
@@ -1800,8 +1801,17 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
       }
       const float inv_tot = 1.f / tot;
       const float inv_own = 1.f / l_run;
+      const float2 ml1 = __ldcg(p.ws_ml + static_cast<long long>(blockIdx.x + 1) * C::BM + rrow);
+      const float w1 = ml1.y * ptx::ex2_approx((ml1.x - mmax) * sl2);  // the first writer's weight
 #pragma unroll 1
       for (int c = 0; c < C::D / 32; ++c) {
+        // The first writer's partial (from L2) is requested before this
+        // piece's own O (from tensor memory), so the two latencies overlap.
+        const float4* src1 = p.ws_o + static_cast<long long>(blockIdx.x + 1) * BLK + rrow +
+                             (c * 8) * C::BM;
+        float4 v1[8];
+#pragma unroll
+        for (int t4 = 0; t4 < 8; ++t4) v1[t4] = __ldcg(src1 + t4 * C::BM);
         uint32_t o[32];
         ptx::tmem_ld32(lane_base + o_col + c * 32, o);
         ptx::tmem_wait_ld();
@@ -1809,8 +1819,15 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
         float acc[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) acc[e] = w_own * (__uint_as_float(o[e]) * inv_own);
+#pragma unroll
+        for (int t4 = 0; t4 < 8; ++t4) {
+          acc[4 * t4 + 0] = fmaf(w1, v1[t4].x, acc[4 * t4 + 0]);
+          acc[4 * t4 + 1] = fmaf(w1, v1[t4].y, acc[4 * t4 + 1]);
+          acc[4 * t4 + 2] = fmaf(w1, v1[t4].z, acc[4 * t4 + 2]);
+          acc[4 * t4 + 3] = fmaf(w1, v1[t4].w, acc[4 * t4 + 3]);
+        }
 #pragma unroll 1
-        for (int q = 1; q <= nw; ++q) {
+        for (int q = 2; q <= nw; ++q) {
           const long long sq = static_cast<long long>(blockIdx.x + q);
           const float2 ml = __ldcg(p.ws_ml + sq * C::BM + rrow);
           const float wq = ml.y * ptx::ex2_approx((ml.x - mmax) * sl2);
@@ -1834,16 +1851,21 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
     } else {
       if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 0);
       const float inv = 1.f / l_run;
+      // 64 columns per tensor-memory round trip.
 #pragma unroll 1
-      for (int c = 0; c < C::D / 32; ++c) {
-        uint32_t o[32];
-        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+      for (int c = 0; c < C::D / 32; c += 2) {
+        uint32_t o[64];
+        ptx::tmem_ld32(lane_base + o_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+        ptx::tmem_ld32(lane_base + o_col + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
         ptx::tmem_wait_ld();
         ptx::reg_fence(o);
-        float v[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]) * inv;
-        store32t(obase, row_g0, c, v);
+        for (int hh = 0; hh < 2; ++hh) {
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[32 * hh + e]) * inv;
+          store32t(obase, row_g0, c + hh, v);
+        }
       }
       if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 1);
     }
