@@ -48,7 +48,8 @@ constexpr int auto_stages(int cap = PAIR ? 12 : 8) {
   int best = 0;
   for (int s = 2; s <= cap; ++s) {
     const int bars = ((C2::NUM_BARS + 2 * (s - 2)) * 8 + 15) / 16 * 16;
-    if (C2::OFF_KV + s * C2::KV_TILE_BYTES + (bars > 256 ? bars : 256) + 1024 + 16 <= limit)
+    if (C2::OFF_KV + s * C2::KV_TILE_BYTES + C2::STAGE_BYTES + (bars > 256 ? bars : 256) +
+            1024 + 32 <= limit)
       best = s;
   }
   return best;

@@ -64,6 +64,7 @@ enum : int {
   kSiteDrain = 7,
   kSiteQFree = 8,
   kSiteMerge = 9,
+  kSiteStage = 10,
   kDeviceTimeoutBase = 0x7100,
 };
 
@@ -352,9 +353,21 @@ struct AttnConfig {
   static constexpr int V_BLK_BYTES = BN * 128;
   static constexpr int V_DBLK = DBLK / CTAS;
   static constexpr int KV_BLK_BYTES = BN * 128;
+  // Variants that can run the persistent schedule: two Q tiles with one S
+  // buffer each (the next item's first S follows the last P V like any other
+  // S) and no CTA pair.  (One-tile CTAs with one S buffer, BN = 256, would
+  // spill registers in it.)
+  static constexpr bool PERSIST_OK = NSBUF == 1 && !PAIR && NQ == 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + NQ * Q_TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_KV + STAGES * KV_TILE_BYTES;
+  // Those variants also hold one Q tile's worth of O staging (128B-swizzled,
+  // the TMA store's layout), which the two Q tiles' epilogues take turns on
+  // in the persistent schedule, where the Q slots already hold the next
+  // item's Q.  (It costs the ring a slot: 4 instead of 5 at 256 x 128, D =
+  // 128, which measured the same.)
+  static constexpr int STAGE_BYTES = PERSIST_OK ? Q_TILE_BYTES : 0;
+  static constexpr int OFF_STAGE = OFF_KV + STAGES * KV_TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_STAGE + STAGE_BYTES;
 
   static constexpr int BAR_Q = 0;
   static constexpr int BAR_KV_FULL = BAR_Q + NQ;
@@ -408,14 +421,11 @@ struct AttnConfig {
   // next item's Q tile i may be loaded over it (one phase per item).
   static constexpr int BAR_Q_FREE = BAR_DRAIN + 1;
   static constexpr int NUM_BARS = BAR_Q_FREE + NQ;
-  // Variants that can run the persistent schedule: two Q tiles with one S
-  // buffer each (the next item's first S follows the last P V like any other
-  // S) and no CTA pair.  (One-tile CTAs with one S buffer, BN = 256, would
-  // spill registers in it.)
-  static constexpr bool PERSIST_OK = NSBUF == 1 && !PAIR && NQ == 2;
 
+  // Misc words: TMEM base (0), abort flag (4), the split merge's last-part
+  // flags (8, 12), the O staging lock (16).
   static constexpr int OFF_MISC = OFF_BAR + ((NUM_BARS * 8 + 15) / 16) * 16;
-  static constexpr int SMEM_USED = OFF_MISC + 16;
+  static constexpr int SMEM_USED = OFF_MISC + 32;
   static constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for manual 1024 B alignment
 
   // Warp roles.
@@ -1648,16 +1658,19 @@ __device__ void mma_role_persistent(uint32_t tmem, uint32_t sbase, const AttnPar
 }
 
 // Softmax warpgroup of Q tile qi over the CTA's items, with each item's
-// epilogue: a whole unit stores O; a kWriter piece writes its normalised
-// partial O and (row max, row sum) into its CTA's workspace slot and counts
-// in on the merging CTA's counter; the kMerger piece waits for its unit's
-// writers, adds their partials to its own in key order and stores O.
-// Every decision that guards a named barrier is taken by all 128 threads
-// together (named_bar_and).
+// epilogue: a whole unit normalises O into the CTA's O staging buffer and
+// stores it with TMA; a kWriter piece writes its normalised partial O and
+// (row max, row sum) into its CTA's workspace slot and counts in on the
+// merging CTA's counter; the kMerger piece waits for its unit's writers,
+// adds their partials to its own in key order and stores O as a whole unit
+// does.  The two Q tiles take turns on the staging buffer (a lock in shared
+// memory, held from the first write into the buffer until the TMA store
+// has read it).  Every decision that guards a named barrier is taken by all
+// 128 threads together (named_bar_and).
 template <typename T, class C, bool PROFILE>
-__device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
-                                        const AttnParams& p, const WaitCtx& w,
-                                        const Prof<PROFILE>& prof) {
+__device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sgen,
+                                        const CUtensorMap* tmO, const AttnParams& p,
+                                        const WaitCtx& w, const Prof<PROFILE>& prof) {
   auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
   const int wi = (threadIdx.x / 32) & 3;
   const int lane = threadIdx.x & 31;
@@ -1669,46 +1682,55 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
   const bool rec = PROFILE && qi == 0 && wi == 0 && lane == 0;
   const uint32_t nbar = 1 + qi;
   constexpr int BLK = C::BM * C::D / 4;  // float4 per workspace slot
+  int* stage_lock = reinterpret_cast<int*>(sgen + C::OFF_MISC + 16);
+  uint8_t* stage_g = sgen + C::OFF_STAGE;
+  const uint32_t stage_s = sbase + C::OFF_STAGE;
 
-  // Stores columns 32c .. 32c + 31 of O for the rows of this thread's group
-  // of four lanes: the four 16-byte chunks of each lane's row are first
-  // transposed across the group (a two-stage butterfly of shuffles), so
-  // that lane b of the group holds chunk 4c + b of each of the group's four
-  // rows and each store instruction writes 64 contiguous bytes of eight rows
-  // instead of 16 bytes of 32.  Rows >= S are not written.  Every lane of
-  // the warp takes part.
-  auto store32t = [&](T* obase, long long row_g0, int c, const float* v) {
-    uint4 x[4];
+  // Writes 16 values (columns 16b .. 16b + 15 of this thread's row) into the
+  // 128B-swizzled staging tile (the layout of the TMA box {64, 128}).
+  auto stage16 = [&](int b, const float* v) {
+    const int dblk = (b * 16) / 64;
+    const int chunk0 = ((b * 16) % 64) / 8;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      x[q].x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
-      x[q].y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
-      x[q].z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
-      x[q].w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+    for (int q = 0; q < 2; ++q) {
+      uint4 u;
+      u.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+      u.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+      u.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+      u.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+      const int chunk = (chunk0 + q) ^ (row & 7);
+      *reinterpret_cast<uint4*>(stage_g + dblk * C::Q_BLK_BYTES + row * 128 + chunk * 16) = u;
     }
-    const int b = lane & 3;
-#pragma unroll
-    for (int m = 1; m < 4; m <<= 1) {
-      const bool hi = (b & m) != 0;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (q & m) continue;
-        const uint4 snd = hi ? x[q] : x[q | m];
-        uint4 r;
-        r.x = __shfl_xor_sync(0xffffffffu, snd.x, m);
-        r.y = __shfl_xor_sync(0xffffffffu, snd.y, m);
-        r.z = __shfl_xor_sync(0xffffffffu, snd.z, m);
-        r.w = __shfl_xor_sync(0xffffffffu, snd.w, m);
-        if (hi)
-          x[q] = r;
-        else
-          x[q | m] = r;
+  };
+  // One thread takes the staging lock (bounded wait).
+  auto take_stage = [&]() -> bool {
+    const unsigned long long t0 = ptx::globaltimer_ns();
+    while (atomicCAS(stage_lock, 0, 1) != 0) {
+      if (*w.abort) return false;
+      if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
+        *w.abort = 1;
+        if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + kSiteStage);
+        return false;
       }
     }
+    return true;
+  };
+  // After the staging writes: one thread stores the tile with TMA (rows >= S
+  // are clipped by the tensor map), waits until the TMA has read the buffer
+  // and releases the lock; the others go on at once.
+  auto store_staged = [&](const Item& x, bool last_rec) {
+    ptx::fence_proxy_async_smem();
+    ptx::named_bar_sync(nbar, 128);
+    if (row == 0) {
+      if (last_rec) prof.stamp(kPhEpilogue, kEpStore, 0);
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (row_g0 + j < p.S)
-        *reinterpret_cast<uint4*>(obase + (row_g0 + j) * C::D + (4 * c + b) * 8) = x[j];
+      for (int d = 0; d < C::DBLK; ++d)
+        ptx::tma_store_3d(tmO, stage_s + d * C::Q_BLK_BYTES, d * 64, x.q_row0 + qi * C::QROWS, x.bh);
+      ptx::tma_store_commit();
+      ptx::tma_store_wait_read0();
+      atomicExch(stage_lock, 0);
+      if (last_rec) prof.stamp(kPhEpilogue, kEpStore, 1);
+    }
   };
 
   ItemCursor cur;
@@ -1722,22 +1744,19 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
     const bool ok = softmax_steps<T, C, PROFILE>(qi, tmem, sbase, p, w, prof, it.kv_lo, it.n, J,
                                                  0, m_run, l_run);
     J += it.n;
-    if (rec && item == 0) prof.stamp(kPhEpilogue, kEpAll, 0);
+    const bool rec0 = rec && item == 0;
+    if (rec0) prof.stamp(kPhEpilogue, kEpAll, 0);
     go = ptx::named_bar_and(nbar, 128, ok && *w.abort == 0);
     if (!go) break;
-    if (rec && item == 0) prof.stamp(kPhEpilogue, kEpWaitO, 0);
+    if (rec0) prof.stamp(kPhEpilogue, kEpWaitO, 0);
     bool fin = wait_bar(bar(C::BAR_O_FINAL + qi), static_cast<uint32_t>(item & 1), w, kSiteODone);
     go = ptx::named_bar_and(nbar, 128, fin);
-    if (rec && item == 0) prof.stamp(kPhEpilogue, kEpWaitO, 1);
+    if (rec0) prof.stamp(kPhEpilogue, kEpWaitO, 1);
     if (!go) break;
     ptx::tc_fence_after();
 
-    // O rows of this thread's group of four lanes start at row_g0.
-    T* obase = static_cast<T*>(p.o_ptr) + it.bh * p.o_head_elems;
-    const long long row_g0 = static_cast<long long>(it.q_row0) + qi * C::QROWS + (row & ~3);
-
     if (it.role == kWriter) {
-      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpPartial, 0);
+      if (rec0) prof.stamp(kPhEpilogue, kEpPartial, 0);
       // Normalised partial O as float4 columns of this CTA's slot: the 32
       // lanes of a warp (32 consecutive rows) write 512 contiguous bytes.
       const float inv = 1.f / l_run;
@@ -1756,120 +1775,106 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase,
               __uint_as_float(o[4 * t4 + 2]) * inv, __uint_as_float(o[4 * t4 + 3]) * inv);
       }
       p.ws_ml[static_cast<long long>(blockIdx.x) * C::BM + rrow] = make_float2(m_run, l_run);
-      __threadfence();
-      ptx::named_bar_sync(nbar, 128);
-      if (row == 0) atomicAdd(p.ws_cnt + it.peer * C::NQ + qi, 1);
-      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpPartial, 1);
-    } else if (it.role == kMerger) {
-      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpCount, 0);
-      const int nw = it.peer - static_cast<int>(blockIdx.x);  // writers: the next nw CTAs
+      // Every thread counts itself in with release semantics: its own
+      // partial is visible to the merger before its increment is.
+      ptx::red_release_gpu_add(p.ws_cnt + it.peer * C::NQ + qi, 1);
+      if (rec0) prof.stamp(kPhEpilogue, kEpPartial, 1);
+    } else {
+      const bool merge = it.role == kMerger;
+      const int nw = merge ? it.peer - static_cast<int>(blockIdx.x) : 0;  // writers: next nw CTAs
       int* cnt = p.ws_cnt + static_cast<int>(blockIdx.x) * C::NQ + qi;
+      if (rec0) prof.stamp(kPhEpilogue, kEpCount, 0);
       bool ready = true;
       if (row == 0) {
-        const unsigned long long t0 = ptx::globaltimer_ns();
-        while (ptx::ld_acquire_gpu(cnt) < nw) {
-          if (*w.abort) {
-            ready = false;
-            break;
-          }
-          if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
-            *w.abort = 1;
-            if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + kSiteMerge);
-            ready = false;
-            break;
+        // The writers' 128 threads each count in once.
+        if (merge) {
+          const unsigned long long t0 = ptx::globaltimer_ns();
+          while (ptx::ld_acquire_gpu(cnt) < nw * 128) {
+            if (*w.abort) {
+              ready = false;
+              break;
+            }
+            if (ptx::globaltimer_ns() - t0 > w.timeout_ns) {
+              *w.abort = 1;
+              if (w.status) atomicCAS(w.status, 0, kDeviceTimeoutBase + kSiteMerge);
+              ready = false;
+              break;
+            }
           }
         }
-        __threadfence();
+        if (ready) ready = take_stage();
       }
       go = ptx::named_bar_and(nbar, 128, ready);
-      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpCount, 1);
+      if (rec0) prof.stamp(kPhEpilogue, kEpCount, 1);
       if (!go) break;
-      if (row == 0) *cnt = 0;  // ready for the next launch (only this CTA reads it)
-      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 0);
-      // Weights of the pieces in key order (own piece first), as the classic
-      // merge computes them: w_q = l_q 2^((m_q - m) scale), m their max.
-      float mmax = m_run;
+      if (rec0) prof.stamp(kPhEpilogue, kEpMerge, 0);
+      if (merge) {
+        if (row == 0) *cnt = 0;  // ready for the next launch (only this CTA reads it)
+        // Weights of the pieces in key order (own piece first), as the
+        // classic merge computes them: w_q = l_q 2^((m_q - m) scale), m
+        // their max.
+        float mmax = m_run;
 #pragma unroll 1
-      for (int q = 1; q <= nw; ++q)
-        mmax = fmaxf(mmax, __ldcg(p.ws_ml + static_cast<long long>(blockIdx.x + q) * C::BM + rrow).x);
-      const float w_own = l_run * ptx::ex2_approx((m_run - mmax) * sl2);
-      float tot = w_own;
+        for (int q = 1; q <= nw; ++q)
+          mmax = fmaxf(mmax, __ldcg(p.ws_ml + static_cast<long long>(blockIdx.x + q) * C::BM + rrow).x);
+        const float w_own = l_run * ptx::ex2_approx((m_run - mmax) * sl2);
+        float tot = w_own;
 #pragma unroll 1
-      for (int q = 1; q <= nw; ++q) {
-        const float2 ml = __ldcg(p.ws_ml + static_cast<long long>(blockIdx.x + q) * C::BM + rrow);
-        tot += ml.y * ptx::ex2_approx((ml.x - mmax) * sl2);
-      }
-      const float inv_tot = 1.f / tot;
-      const float inv_own = 1.f / l_run;
-      const float2 ml1 = __ldcg(p.ws_ml + static_cast<long long>(blockIdx.x + 1) * C::BM + rrow);
-      const float w1 = ml1.y * ptx::ex2_approx((ml1.x - mmax) * sl2);  // the first writer's weight
-#pragma unroll 1
-      for (int c = 0; c < C::D / 32; ++c) {
-        // The first writer's partial (from L2) is requested before this
-        // piece's own O (from tensor memory), so the two latencies overlap.
-        const float4* src1 = p.ws_o + static_cast<long long>(blockIdx.x + 1) * BLK + rrow +
-                             (c * 8) * C::BM;
-        float4 v1[8];
-#pragma unroll
-        for (int t4 = 0; t4 < 8; ++t4) v1[t4] = __ldcg(src1 + t4 * C::BM);
-        uint32_t o[32];
-        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
-        ptx::tmem_wait_ld();
-        ptx::reg_fence(o);
-        float acc[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) acc[e] = w_own * (__uint_as_float(o[e]) * inv_own);
-#pragma unroll
-        for (int t4 = 0; t4 < 8; ++t4) {
-          acc[4 * t4 + 0] = fmaf(w1, v1[t4].x, acc[4 * t4 + 0]);
-          acc[4 * t4 + 1] = fmaf(w1, v1[t4].y, acc[4 * t4 + 1]);
-          acc[4 * t4 + 2] = fmaf(w1, v1[t4].z, acc[4 * t4 + 2]);
-          acc[4 * t4 + 3] = fmaf(w1, v1[t4].w, acc[4 * t4 + 3]);
+        for (int q = 1; q <= nw; ++q) {
+          const float2 ml = __ldcg(p.ws_ml + static_cast<long long>(blockIdx.x + q) * C::BM + rrow);
+          tot += ml.y * ptx::ex2_approx((ml.x - mmax) * sl2);
         }
+        const float inv_tot = 1.f / tot;
+        const float inv_own = 1.f / l_run;
 #pragma unroll 1
-        for (int q = 2; q <= nw; ++q) {
-          const long long sq = static_cast<long long>(blockIdx.x + q);
-          const float2 ml = __ldcg(p.ws_ml + sq * C::BM + rrow);
-          const float wq = ml.y * ptx::ex2_approx((ml.x - mmax) * sl2);
-          const float4* src = p.ws_o + sq * BLK + rrow + (c * 8) * C::BM;
-          float4 v[8];
+        for (int b = 0; b < C::D / 16; ++b) {
+          uint32_t o[16];
+          ptx::tmem_ld16(lane_base + o_col + b * 16, o);
+          ptx::tmem_wait_ld();
+          ptx::reg_fence(o);
+          float acc[16];
 #pragma unroll
-          for (int t4 = 0; t4 < 8; ++t4) v[t4] = __ldcg(src + t4 * C::BM);
+          for (int e = 0; e < 16; ++e) acc[e] = w_own * (__uint_as_float(o[e]) * inv_own);
+#pragma unroll 1
+          for (int q = 1; q <= nw; ++q) {
+            const long long sq = static_cast<long long>(blockIdx.x + q);
+            const float2 ml = __ldcg(p.ws_ml + sq * C::BM + rrow);
+            const float wq = ml.y * ptx::ex2_approx((ml.x - mmax) * sl2);
+            const float4* src = p.ws_o + sq * BLK + rrow + (b * 4) * C::BM;
+            float4 v[4];
 #pragma unroll
-          for (int t4 = 0; t4 < 8; ++t4) {
-            acc[4 * t4 + 0] = fmaf(wq, v[t4].x, acc[4 * t4 + 0]);
-            acc[4 * t4 + 1] = fmaf(wq, v[t4].y, acc[4 * t4 + 1]);
-            acc[4 * t4 + 2] = fmaf(wq, v[t4].z, acc[4 * t4 + 2]);
-            acc[4 * t4 + 3] = fmaf(wq, v[t4].w, acc[4 * t4 + 3]);
+            for (int t4 = 0; t4 < 4; ++t4) v[t4] = __ldcg(src + t4 * C::BM);
+#pragma unroll
+            for (int t4 = 0; t4 < 4; ++t4) {
+              acc[4 * t4 + 0] = fmaf(wq, v[t4].x, acc[4 * t4 + 0]);
+              acc[4 * t4 + 1] = fmaf(wq, v[t4].y, acc[4 * t4 + 1]);
+              acc[4 * t4 + 2] = fmaf(wq, v[t4].z, acc[4 * t4 + 2]);
+              acc[4 * t4 + 3] = fmaf(wq, v[t4].w, acc[4 * t4 + 3]);
+            }
           }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) acc[e] *= inv_tot;
+          stage16(b, acc);
         }
-#pragma unroll
-        for (int e = 0; e < 32; ++e) acc[e] *= inv_tot;
-        store32t(obase, row_g0, c, acc);
-      }
-      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 1);
-    } else {
-      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 0);
-      const float inv = 1.f / l_run;
-      // 64 columns per tensor-memory round trip.
+      } else {
+        const float inv = 1.f / l_run;
 #pragma unroll 1
-      for (int c = 0; c < C::D / 32; c += 2) {
-        uint32_t o[64];
-        ptx::tmem_ld32(lane_base + o_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-        ptx::tmem_ld32(lane_base + o_col + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
-        ptx::tmem_wait_ld();
-        ptx::reg_fence(o);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int c = 0; c < C::D / 32; ++c) {
+          uint32_t o[32];
+          ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+          ptx::tmem_wait_ld();
+          ptx::reg_fence(o);
           float v[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[32 * hh + e]) * inv;
-          store32t(obase, row_g0, c + hh, v);
+          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]) * inv;
+          stage16(2 * c, v);
+          stage16(2 * c + 1, v + 16);
         }
       }
-      if (rec && item == 0) prof.stamp(kPhEpilogue, kEpMerge, 1);
+      if (rec0) prof.stamp(kPhEpilogue, kEpMerge, 1);
+      store_staged(it, rec0);
     }
-    if (rec && item == 0) prof.stamp(kPhEpilogue, kEpAll, 1);
+    if (rec0) prof.stamp(kPhEpilogue, kEpAll, 1);
     ++item;
   }
 }
@@ -1927,6 +1932,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_TH
     }
     ptx::mbar_init(bar(C::BAR_DRAIN), C::NUM_ISSUERS);
     *abort_flag = 0;
+    *reinterpret_cast<volatile int*>(sgen + C::OFF_MISC + 16) = 0;  // O staging lock
     ptx::fence_mbar_init();
   }
   if (warp == C::LOAD_WARP && lane == 0) {
@@ -1954,7 +1960,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_TH
     {
       if (warp < C::NUM_SOFTMAX_WARPS) {
         if constexpr (C::NQ == 2) ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
-        softmax_role_persistent<T, C, PROFILE>(warp / 4, tmem, sbase, p, w, prof);
+        softmax_role_persistent<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, p, w, prof);
       } else {
         if constexpr (C::NQ == 2) ptx::setmaxnreg_dec<C::REG_OTHER>();
         if (warp == C::LOAD_WARP) {

@@ -123,8 +123,16 @@ __device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bo
   return r != 0;
 }
 
+// Atomic add to a global int with release semantics at GPU scope: this
+// thread's earlier writes are visible to any thread that observes the add
+// with an acquire load.
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Load of a global int with acquire semantics at GPU scope (pairs with a
-// release -- __threadfence() then atomicAdd -- in another CTA).
+// release -- red_release_gpu_add, or __threadfence() then atomicAdd -- in
+// another CTA).
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -43,10 +43,11 @@ def smem_bytes(BM: int, BN: int, HD: int, stages: int) -> int:
     nsbuf = 2 if nq * (2 * BN + HD) <= TMEM_COLS else 1
     exp_bound = nq == 2 and HD == 64 and nq * (2 * BN + HD) <= TMEM_COLS
     phalves = 2 if (BN >= 64 and not exp_bound) else 1
-    off_bar = nq * 128 * HD * 2 + stages * BN * HD * 2
+    stage = 128 * HD * 2 if (nq == 2 and nsbuf == 1) else 0  # O staging (persistent tiles)
+    off_bar = nq * 128 * HD * 2 + stages * BN * HD * 2 + stage
     num_bars = nq + 2 * stages + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1 + nq
     off_misc = off_bar + ((num_bars * 8 + 15) // 16) * 16
-    return off_misc + 16 + 1024
+    return off_misc + 32 + 1024
 
 
 def lib_stages(BM: int, BN: int, HD: int, cap: int = 8) -> int:
@@ -61,10 +62,11 @@ def lib_stages(BM: int, BN: int, HD: int, cap: int = 8) -> int:
     phalves = 2 if (BN >= 64 and not exp_bound) else 1
     bars2 = nq + 2 * 2 + nq * nsbuf + nq * nsbuf * phalves + 2 * nq + 1 + nq
     off_kv = nq * 128 * HD * 2
+    stage = 128 * HD * 2 if (nq == 2 and nsbuf == 1) else 0
     best = 0
     for s in range(2, cap + 1):
         bars = ((bars2 + 2 * (s - 2)) * 8 + 15) // 16 * 16
-        if off_kv + s * BN * HD * 2 + max(bars, 256) + 1024 + 16 <= limit:
+        if off_kv + s * BN * HD * 2 + stage + max(bars, 256) + 1024 + 32 <= limit:
             best = s
     return best
 

@@ -49,12 +49,13 @@ def test_solver_matches_library_geometry(engine):
 
 def test_pair_tile_geometry(engine):
     """BM = 512 (CTA pairs, D = 128 only): each CTA holds two Q tiles and
-    half-size K/V slots, so the ring is twice as deep as at BM = 256."""
+    half-size K/V slots, so the ring is at least twice as deep as at BM = 256
+    (whose CTA also holds the persistent schedule's O staging)."""
     for BM, BN in engine.PAIR_TILES:
         q = engine.query_config(128, BM, BN, 0)
         single = engine.query_config(128, 256, BN, 0)
         assert q["num_threads"] == single["num_threads"] and q["tmem_cols"] == 512
-        assert q["stages"] == 2 * single["stages"] and q["smem_bytes"] <= 232448
+        assert q["stages"] >= 2 * single["stages"] and q["smem_bytes"] <= 232448
         with pytest.raises(engine.AttnError):
             engine.query_config(64, BM, BN, 0)
 
