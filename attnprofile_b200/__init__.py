@@ -226,16 +226,17 @@ def set_split(mode: int) -> None:
 
 
 def set_schedule(mode: int) -> None:
-    """Schedule of later launches: 0 automatic (default), 1 classic (one CTA
-    per unit), 2 persistent wherever the tile has it (one resident CTA per
-    SM slot sharing the launch's (unit, key tile) steps)."""
+    """Schedule of later launches: 0 automatic (default; runs the classic
+    schedule), 1 classic (one CTA per unit), 2 persistent wherever the tile
+    has it (one resident CTA per SM slot sharing the launch's (unit, key
+    tile) steps)."""
     _check(lib().attn_set_schedule(int(mode)), "attn_set_schedule")
 
 
 def plan_schedule(units: int, num_kv_tiles: int, slots: int) -> dict:
-    """The host planner alone (no GPU): the automatic choice between the
-    persistent and the classic schedule, the persistent grid and the most
-    pieces a unit is cut into, with both modelled costs."""
+    """The host planner alone (no GPU): whether the automatic mode picks the
+    persistent schedule (it does not), the persistent grid and the most
+    pieces a unit is cut into, with both schedules' modelled costs."""
     pers, ctas, pieces = ctypes.c_int(), ctypes.c_longlong(), ctypes.c_int()
     cp, cc = ctypes.c_double(), ctypes.c_double()
     _check(lib().attn_plan_schedule(units, num_kv_tiles, slots, ctypes.byref(pers),

@@ -422,18 +422,18 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   const int n_kv = (S + BN - 1) / BN;
   SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, PAIR ? 1 : o.split);
   plan_workspace(&plan, C::BM, D, NQ, sizeof(float));
-  // Persistent schedule: where the variant has it, the split mode is
-  // automatic (attn_set_split 0) and the schedule mode allows it; in
-  // automatic mode when its model is no slower than the classic plan's.
-  // (A CTA's steps are counted in 32 bits.)
-  if (C::PERSIST_OK && o.split == 0 && o.schedule != 1 && BH * qt > 0 &&
+  // Persistent schedule: only when asked for (attn_set_schedule(2)), where
+  // the variant has it and the split mode is automatic.  The automatic mode
+  // runs the classic plan: on a B200 the persistent schedule measured within
+  // -3 .. +2 % of it on the benchmark shapes and slower on few long units
+  // (its per-CTA partial writes, merges and item boundaries cost about what
+  // the classic grid's last wave leaves idle).  (A CTA's steps are counted
+  // in 32 bits.)
+  if (C::PERSIST_OK && o.split == 0 && o.schedule == 2 && BH * qt > 0 &&
       BH * qt * n_kv / slots < (1ll << 29)) {
     SplitPlan pp = plan_persistent(BH * qt, n_kv, slots);
-    if (o.schedule == 2 ||
-        persistent_cost(BH * qt, n_kv, pp.ctas) <= classic_cost(plan, n_kv, slots)) {
-      plan_workspace_persistent(&pp, C::BM, D, NQ);
-      plan = pp;
-    }
+    plan_workspace_persistent(&pp, C::BM, D, NQ);
+    plan = pp;
   }
   if (o.plan_out) *o.plan_out = plan;
   if (o.plan_only) return ATTN_OK;

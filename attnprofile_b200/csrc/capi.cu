@@ -308,7 +308,7 @@ int attn_plan_schedule(long long units, int num_kv_tiles, long long slots, int* 
   const SplitPlan pp = plan_persistent(units, num_kv_tiles, slots);
   const double cp = persistent_cost(units, num_kv_tiles, pp.ctas);
   const double cc = classic_cost(cl, num_kv_tiles, slots);
-  if (persistent) *persistent = cp <= cc ? 1 : 0;
+  if (persistent) *persistent = 0;  // the automatic mode runs the classic plan
   if (ctas) *ctas = pp.ctas;
   if (pieces) *pieces = pp.split;
   if (persistent_cost_out) *persistent_cost_out = cp;

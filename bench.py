@@ -561,8 +561,10 @@ def main():
                          "kernel": "attn_fwd_kernel"},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
-            "schedule": ap.query_split(cfg["B"], w["H"], S, D, BM=args.bm, BN=args.bn,
-                                       dtype=0 if w["dtype"] == "f16" else 1),
+            "plan": dict(ap.query_split(cfg["B"], w["H"], S, D, BM=args.bm, BN=args.bn,
+                                        dtype=0 if w["dtype"] == "f16" else 1),
+                         schedule={0: "automatic (classic)", 1: "classic",
+                                   2: "persistent"}[args.schedule]),
         }
         line.update(subs)
         if gather is not None:

@@ -168,14 +168,16 @@ int attn_set_split(int mode);
  *               first key tile, which adds the other pieces' partial results
  *               (written by the next CTAs first) in key order.  Launched
  *               cooperatively (all CTAs resident at once).
- * attn_set_schedule -- mode 0 automatic (persistent where the variant has it
- *   and its cost model is no slower; only with the automatic split mode),
- *   1 classic only, 2 persistent whenever the variant has it.
- * attn_plan_schedule -- the host planner alone (no GPU): whether the
- *   automatic mode picks the persistent schedule for U units of
- *   num_kv_tiles key tiles on `slots` resident CTAs, its grid, the most
- *   pieces a unit is cut into, and both schedules' modelled costs (in
- *   key-tile periods of one CTA).
+ * attn_set_schedule -- mode 0 automatic, 1 classic, 2 persistent whenever
+ *   the variant has it (and the split mode is automatic).  The automatic
+ *   mode runs the classic schedule: on a B200 the persistent one measured
+ *   within -3 .. +2 % of it on the benchmark shapes and slower on shapes of
+ *   few long units, so it is opt-in.
+ * attn_plan_schedule -- the host planner alone (no GPU): for U units of
+ *   num_kv_tiles key tiles on `slots` resident CTAs, whether the automatic
+ *   mode picks the persistent schedule (it does not), the persistent grid,
+ *   the most pieces a unit is cut into, and both schedules' modelled costs
+ *   (in key-tile periods of one CTA).
  * No counterpart in the reference, whose grid is one CTA per unit
  * (tuning/attn_test.cu:1583-1663).
  */

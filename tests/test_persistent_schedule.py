@@ -115,9 +115,9 @@ def test_host_planner_matches_the_model(engine, U, nkv, slots):
         for it in items_of(c, U, nkv, G):
             per_unit[it["u"]] = per_unit.get(it["u"], 0) + 1
     assert plan["pieces"] == max(per_unit.values())
-    # the benchmark shapes take the persistent schedule
-    if (U, nkv, slots) in ((256, 32, 148), (8192, 64, 148)):
-        assert plan["persistent"] and plan["persistent_cost"] < plan["classic_cost"]
+    # the automatic mode runs the classic schedule (measured no slower)
+    assert plan["persistent"] is False
+    assert plan["persistent_cost"] > 0 and plan["classic_cost"] > 0
 
 
 # ---------------------------------------------------------------------------
