@@ -15,6 +15,8 @@ recompilation: the C ABI dispatches them at run time.
 
     python -m attnprofile_b200.ncu_sweep --seq-lens 4096 --head-dims 64,128 \\
         --tiles 256x128,256x64,128x128 --out profiles/ncu_sweep.csv
+    python -m attnprofile_b200.ncu_sweep --shapes 1x32x8192x128:bf16,1x8x32768x128 \\
+        --tiles 256x128 --out shards.csv        # explicit shapes, f16 unless :bf16
 
 Run it on one GPU; every capture is one launch of a small problem (a few
 passes of ~0.1 ms kernels).
@@ -37,21 +39,24 @@ METRICS = {
     "sm__inst_executed_pipe_xu.avg.pct_of_peak_sustained_active": "xu_utilization",
     "smsp__issue_active.avg.pct_of_peak_sustained_active": "issue_active",
     "dram__bytes_read.sum": "dram_read_bytes",
+    "dram__bytes_write.sum": "dram_write_bytes",
     "l1tex__data_pipe_tc_wavefronts_mem_shared.sum.pct_of_peak_sustained_elapsed": "tc_smem_pct",
 }
-CSV_FIELDS = ["B", "H", "S", "D", "BM", "BN", "time", "tflops", "tc_utilization",
-              "xu_utilization", "issue_active", "dram_read_bytes", "tc_smem_pct"]
+CSV_FIELDS = ["B", "H", "S", "D", "dtype", "BM", "BN", "time", "tflops", "tc_utilization",
+              "xu_utilization", "issue_active", "dram_read_bytes", "dram_write_bytes",
+              "tc_smem_pct"]
 UNIT_SCALE = {"ns": 1e-6, "nsecond": 1e-6, "us": 1e-3, "usecond": 1e-3, "ms": 1.0, "msecond": 1.0,
               "s": 1e3, "second": 1e3, "byte": 1.0, "kbyte": 1e3, "mbyte": 1e6, "gbyte": 1e9, "%": 1.0}
 
 
-def child(B: int, H: int, S: int, D: int, BM: int, BN: int) -> int:
+def child(B: int, H: int, S: int, D: int, BM: int, BN: int, bf16: int = 0) -> int:
     """Three launches (two warm-up, the third captured) of one tile."""
     import torch
 
     import attnprofile_b200 as ap
     g = torch.Generator(device="cuda").manual_seed(B * 1000 + H * 10 + D)
-    Q, K, V = (torch.randn(B, H, S, D, generator=g, device="cuda").half() for _ in range(3))
+    dt = torch.bfloat16 if bf16 else torch.float16
+    Q, K, V = (torch.randn(B, H, S, D, generator=g, device="cuda").to(dt) for _ in range(3))
     O = torch.empty_like(Q)
     for _ in range(3):
         ap.attn(Q, K, V, O, BM=BM, BN=BN)
@@ -84,10 +89,11 @@ def parse_ncu_csv(text: str) -> dict:
 
 
 def profile(ncu: str, shape, tile, timeout: float) -> dict | None:
-    B, H, S, D = shape
+    B, H, S, D = shape[:4]
+    dtype = shape[4] if len(shape) > 4 else "f16"
     BM, BN = tile
     cmd = [sys.executable, "-m", "attnprofile_b200.ncu_sweep", "--child",
-           *map(str, (B, H, S, D, BM, BN))]
+           *map(str, (B, H, S, D, BM, BN, 1 if dtype == "bf16" else 0))]
     env = dict(os.environ)
     plain = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
     if plain.returncode != 0:
@@ -100,7 +106,7 @@ def profile(ncu: str, shape, tile, timeout: float) -> dict | None:
     m = parse_ncu_csv(prof.stdout)
     if "time" not in m:
         return None
-    row = {"B": B, "H": H, "S": S, "D": D, "BM": BM, "BN": BN}
+    row = {"B": B, "H": H, "S": S, "D": D, "dtype": dtype, "BM": BM, "BN": BN}
     row.update({k: m.get(k, math.nan) for k in CSV_FIELDS if k in METRICS.values()})
     row["tflops"] = 4.0 * B * H * S * S * D / (m["time"] * 1e-3) / 1e12
     return row
@@ -110,9 +116,25 @@ def ints(v: str):
     return [int(x) for x in v.replace(" ", ",").split(",") if x.strip()]
 
 
+def parse_shapes(v: str):
+    """'1x32x8192x128:bf16,1x8x32768x128' -> [(1, 32, 8192, 128, 'bf16'), (1, 8, 32768, 128, 'f16')]."""
+    out = []
+    for item in v.split(","):
+        if not item.strip():
+            continue
+        dims, _, dt = item.strip().partition(":")
+        B, H, S, D = (int(x) for x in dims.split("x"))
+        if (dt or "f16") not in ("f16", "bf16"):
+            raise ValueError(f"dtype must be f16 or bf16, got {dt!r}")
+        out.append((B, H, S, D, dt or "f16"))
+    return out
+
+
 def main(argv=None) -> int:
     ap_ = argparse.ArgumentParser()
-    ap_.add_argument("--child", nargs=6, type=int, metavar=("B", "H", "S", "D", "BM", "BN"))
+    ap_.add_argument("--child", nargs=7, type=int, metavar=("B", "H", "S", "D", "BM", "BN", "BF16"))
+    ap_.add_argument("--shapes", default=None,
+                     help="explicit shapes BxHxSxD[:bf16],... (instead of the product of the lists)")
     ap_.add_argument("--batch-sizes", default="1")
     ap_.add_argument("--num-heads", default="16")
     ap_.add_argument("--seq-lens", default="4096")
@@ -125,8 +147,11 @@ def main(argv=None) -> int:
     if a.child:
         return child(*a.child)
     tiles = [tuple(int(x) for x in t.split("x")) for t in a.tiles.split(",")]
-    shapes = list(itertools.product(ints(a.batch_sizes), ints(a.num_heads), ints(a.seq_lens),
-                                    ints(a.head_dims)))
+    if a.shapes:
+        shapes = parse_shapes(a.shapes)
+    else:
+        shapes = list(itertools.product(ints(a.batch_sizes), ints(a.num_heads), ints(a.seq_lens),
+                                        ints(a.head_dims)))
     out = Path(a.out)
     with out.open("w", newline="") as f:
         csv.DictWriter(f, fieldnames=CSV_FIELDS).writeheader()

@@ -21,3 +21,8 @@ def test_parse_ncu_csv_units():
 
 def test_parse_ncu_csv_empty():
     assert ncu_sweep.parse_ncu_csv("no csv here") == {}
+
+
+def test_parse_shapes():
+    assert ncu_sweep.parse_shapes("1x32x8192x128:bf16, 1x8x32768x128") == [
+        (1, 32, 8192, 128, "bf16"), (1, 8, 32768, 128, "f16")]
