@@ -19,6 +19,7 @@ __all__ = [
     "set_timeout_ns", "debug_fault", "lib", "build", "ERR", "SUPPORTED_TILES", "PAIR_TILES",
     "attn_sharded",
     "shard_range", "set_split", "set_schedule", "plan_split", "plan_schedule", "query_split",
+    "set_correction",
 ]
 
 ERR = {
@@ -75,6 +76,7 @@ def lib() -> ctypes.CDLL:
         ll, llp = ctypes.c_longlong, ctypes.POINTER(ctypes.c_longlong)
         L.attn_set_split.argtypes = [i]
         L.attn_set_schedule.argtypes = [i]
+        L.attn_set_correction.argtypes = [i]
         L.attn_plan_schedule.argtypes = [ll, i, ll, ctypes.POINTER(i), llp, ctypes.POINTER(i),
                                          ctypes.POINTER(ctypes.c_double),
                                          ctypes.POINTER(ctypes.c_double)]
@@ -84,7 +86,7 @@ def lib() -> ctypes.CDLL:
                      "attn_shard_range", "attn_get_status", "attn_query_config",
                      "attn_profile_layout", "attn_debug_fault", "attn_version",
                      "attn_set_split", "attn_plan_split", "attn_query_split",
-                     "attn_set_schedule", "attn_plan_schedule"):
+                     "attn_set_schedule", "attn_plan_schedule", "attn_set_correction"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -231,6 +233,14 @@ def set_schedule(mode: int) -> None:
     has it (one resident CTA per SM slot sharing the launch's (unit, key
     tile) steps)."""
     _check(lib().attn_set_schedule(int(mode)), "attn_set_schedule")
+
+
+def set_correction(mode: int) -> None:
+    """1: later launches run with a correction warpgroup where the tile has
+    one (BM 256 with BN 128, and 256 x 96 at D = 64), which owns the lazy O
+    rescale, the final normalisation and the TMA store of O (classic
+    schedule, no key split); 0 (default): the softmax warpgroups do that."""
+    _check(lib().attn_set_correction(int(mode)), "attn_set_correction")
 
 
 def plan_schedule(units: int, num_kv_tiles: int, slots: int) -> dict:

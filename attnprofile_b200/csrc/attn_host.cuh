@@ -77,6 +77,7 @@ struct LaunchOpts {
   int prof_cta = 0;
   int split = 0;                 // 0: automatic, 1: never split, k >= 2: split k ways
   int schedule = 0;              // 0: automatic, 1: classic only, 2: persistent where built
+  bool corr = false;             // correction-warpgroup kernel where built (whole units)
   void* workspace = nullptr;     // caller-provided workspace (else stream-ordered pool)
   size_t workspace_bytes = 0;
   bool no_pool = false;          // never fall back to the pool: a split plan needs `workspace`
@@ -365,6 +366,13 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   // The persistent schedule's kernel (the classic one again where the
   // variant has no persistent schedule).
   auto kern_p = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE, PAIR, C::PERSIST_OK>;
+  // The classic schedule with a correction warpgroup (the classic kernel
+  // again where the variant has none).
+  constexpr bool kCorr = C::CORR_OK;
+  using CC = AttnConfig<T, D, BN, NQ, STAGES, PAIR, kCorr>;
+  static_assert(CC::SMEM_BYTES <= kSmemLimit, "shared memory over the sm_100 per-CTA limit");
+  auto kern_c = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE, PAIR, false, kCorr>;
+  const bool corr = kCorr && o.corr;
   // CTA pairs run as clusters of two consecutive CTAs.
   cudaLaunchAttribute cluster_attr{};
   cluster_attr.id = cudaLaunchAttributeClusterDimension;
@@ -395,7 +403,9 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
               cudaSuccess ||
           cudaFuncSetAttribute(kern_p, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               C::SMEM_BYTES) != cudaSuccess)
+                               C::SMEM_BYTES) != cudaSuccess ||
+          cudaFuncSetAttribute(kern_c, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               CC::SMEM_BYTES) != cudaSuccess)
         return ATTN_ERR_RESOURCE;
       int sms = 0, occ = 0;
       if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
@@ -420,7 +430,8 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   // unit per cluster; pairs take no key split).
   const long long qt = (S + C::BM * C::CTAS - 1) / (C::BM * C::CTAS);
   const int n_kv = (S + BN - 1) / BN;
-  SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, PAIR ? 1 : o.split);
+  // (The correction-warpgroup kernel stores whole units only: no key split.)
+  SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, (PAIR || corr) ? 1 : o.split);
   plan_workspace(&plan, C::BM, D, NQ, sizeof(float));
   // Persistent schedule: only when asked for (attn_set_schedule(2)), where
   // the variant has it and the split mode is automatic.  The automatic mode
@@ -429,7 +440,7 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   // (its per-CTA partial writes, merges and item boundaries cost about what
   // the classic grid's last wave leaves idle).  (A CTA's steps are counted
   // in 32 bits.)
-  if (C::PERSIST_OK && o.split == 0 && o.schedule == 2 && BH * qt > 0 &&
+  if (C::PERSIST_OK && !corr && o.split == 0 && o.schedule == 2 && BH * qt > 0 &&
       BH * qt * n_kv / slots < (1ll << 29)) {
     SplitPlan pp = plan_persistent(BH * qt, n_kv, slots);
     plan_workspace_persistent(&pp, C::BM, D, NQ);
@@ -507,6 +518,10 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
     if constexpr (PAIR) {
       const cudaLaunchConfig_t cfg = launch_cfg(static_cast<unsigned>(plan.ctas * C::CTAS));
       if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mo, p) != cudaSuccess) rc = ATTN_ERR_CUDA;
+    } else if (corr) {
+      kern_c<<<static_cast<unsigned>(plan.ctas), CC::NUM_THREADS, CC::SMEM_BYTES, stream>>>(
+          mq, mk, mv, mo, p);
+      if (cudaGetLastError() != cudaSuccess) rc = ATTN_ERR_CUDA;
     } else {
       kern<<<static_cast<unsigned>(plan.ctas), C::NUM_THREADS, C::SMEM_BYTES, stream>>>(mq, mk,
                                                                                        mv, mo, p);

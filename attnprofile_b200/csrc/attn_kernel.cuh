@@ -65,6 +65,7 @@ enum : int {
   kSiteQFree = 8,
   kSiteMerge = 9,
   kSiteStage = 10,
+  kSiteCorr = 11,
   kDeviceTimeoutBase = 0x7100,
 };
 
@@ -308,13 +309,18 @@ constexpr bool kJointFull = ATTNPROF_JOINT_FULL != 0;
 // keys) and half of every V tile (D/2 columns), so the per-SM shared-memory
 // traffic of the B operands, the TMA writes and the L2 reads halve and the
 // same ring holds twice as many key tiles.  The even CTA issues all MMAs.
-template <typename T, int D_, int BN_, int NQ_, int STAGES_, bool PAIR_ = false>
+template <typename T, int D_, int BN_, int NQ_, int STAGES_, bool PAIR_ = false, bool CORR_ = false>
 struct AttnConfig {
   static constexpr int D = D_;
   static constexpr int BN = BN_;
   static constexpr int NQ = NQ_;
   static constexpr int STAGES = STAGES_;
   static constexpr bool PAIR = PAIR_;
+  // CORR: a correction warpgroup owns the lazy rescale of both tiles' O in
+  // tensor memory, the final 1 / rowsum normalisation and the TMA store of O;
+  // the softmax warpgroups hand it each step's rescale factors and, after
+  // their last step, the row sums.  Built for two-tile CTAs without pairs.
+  static constexpr bool CORR = CORR_;
   static constexpr int CTAS = PAIR ? 2 : 1;  // CTAs that share one MMA
   static constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
 
@@ -324,6 +330,7 @@ struct AttnConfig {
   static_assert(STAGES >= 2, "need at least two K/V slots");
   static_assert(!PAIR || (D == 128 && BN == 128 && NQ == 2),
                 "CTA pairs are built for D = 128, BN = 128, two Q tiles per CTA");
+  static_assert(!CORR || (NQ == 2 && !PAIR), "the correction warpgroup serves two-tile CTAs");
 
   static constexpr int QROWS = 128;  // rows per Q tile = MMA M = TMEM lanes
   static constexpr int BM = QROWS * NQ;
@@ -357,7 +364,10 @@ struct AttnConfig {
   // buffer each (the next item's first S follows the last P V like any other
   // S) and no CTA pair.  (One-tile CTAs with one S buffer, BN = 256, would
   // spill registers in it.)
-  static constexpr bool PERSIST_OK = NSBUF == 1 && !PAIR && NQ == 2;
+  static constexpr bool PERSIST_OK = NSBUF == 1 && !PAIR && NQ == 2 && !CORR;
+  // Variants that also have the correction-warpgroup kernel (the tiles of
+  // the benchmark configurations).
+  static constexpr bool CORR_OK = NQ == 2 && !PAIR && (BN == 128 || (D == 64 && BN == 96));
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + NQ * Q_TILE_BYTES;
   // Those variants also hold one Q tile's worth of O staging (128B-swizzled,
@@ -367,7 +377,13 @@ struct AttnConfig {
   // 128, which measured the same.)
   static constexpr int STAGE_BYTES = PERSIST_OK ? Q_TILE_BYTES : 0;
   static constexpr int OFF_STAGE = OFF_KV + STAGES * KV_TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_STAGE + STAGE_BYTES;
+  // CORR: per Q tile and S buffer, each row's rescale factor of the step in
+  // that buffer ([NQ][NSBUF][QROWS] floats), then per Q tile each row's sum
+  // ([NQ][QROWS], after the last step).
+  static constexpr int CORR_ALPHA_FLOATS = NQ * NSBUF * QROWS;
+  static constexpr int CORR_BYTES = CORR ? (CORR_ALPHA_FLOATS + NQ * QROWS) * 4 : 0;
+  static constexpr int OFF_CORR = OFF_STAGE + STAGE_BYTES;
+  static constexpr int OFF_BAR = OFF_CORR + CORR_BYTES;
 
   static constexpr int BAR_Q = 0;
   static constexpr int BAR_KV_FULL = BAR_Q + NQ;
@@ -420,7 +436,18 @@ struct AttnConfig {
   // Persistent schedule: the last S of an item has read Q tile i, so the
   // next item's Q tile i may be loaded over it (one phase per item).
   static constexpr int BAR_Q_FREE = BAR_DRAIN + 1;
-  static constexpr int NUM_BARS = BAR_Q_FREE + NQ;
+  // CORR: tile i's softmax warps arrive on BAR_CORR + i * NSBUF + (j mod
+  // NSBUF) at step j (the step's rescale factors are in shared memory), and
+  // on BAR_CORR_END + i after the last step (the row sums are).  Each S
+  // buffer has its own request barrier and factors: with two buffers the
+  // softmax may post step j + 1 (its S was issued before P V of step j)
+  // while the correction warps still serve step j, but not step j + 2 (its S
+  // follows P V of step j, which waits for them).  The end gets a barrier of
+  // its own: the last step's request and the end's follow each other with
+  // nothing in between that waits for the correction warps.
+  static constexpr int BAR_CORR = BAR_Q_FREE + NQ;
+  static constexpr int BAR_CORR_END = BAR_CORR + NQ * NSBUF;
+  static constexpr int NUM_BARS = BAR_CORR + (CORR ? NQ * NSBUF + NQ : 0);
 
   // Misc words: TMEM base (0), abort flag (4), the split merge's last-part
   // flags (8, 12), the O staging lock (16).
@@ -445,17 +472,25 @@ struct AttnConfig {
   // commits.
   static constexpr int NUM_ISSUERS = (NQ == 2 && NSBUF == 2) ? 2 : 1;
   static constexpr int MMA_WARP2 = NUM_SOFTMAX_WARPS + 3;
-  static constexpr int NUM_THREADS = 32 * (NUM_SOFTMAX_WARPS + 4);
+  // CORR: the correction warpgroup is the last four warps; warp w of it
+  // serves TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31, the rows of softmax warp
+  // w % 4 of each tile.
+  static constexpr int CORR_WARP0 = NUM_SOFTMAX_WARPS + 4;
+  static constexpr int NUM_THREADS = 32 * (NUM_SOFTMAX_WARPS + 4 + (CORR ? 4 : 0));
   // One 128-row Q tile with narrow key tiles fits two CTAs per SM (shared
   // and tensor memory); the register budget is capped to keep that possible.
   static constexpr int MIN_CTAS_PER_SM = (NQ == 1 && BN <= 64) ? 2 : 1;
   // Register split for NQ = 2: 384 threads launched at 168 registers each
   // (64512): softmax warpgroups 2 x 128 x 192 + producer/MMA warpgroup
-  // 128 x 120.
+  // 128 x 120.  CORR: 512 threads launched at 128 (65536): softmax
+  // 2 x 128 x 192 + producer/MMA 128 x 72 + correction 128 x 56 (the MMA
+  // issuer spills below 72).
   static constexpr int LAUNCH_REGS = (65536 / NUM_THREADS) & ~7;
   static constexpr uint32_t REG_SOFTMAX = 192;
-  static constexpr uint32_t REG_OTHER = 120;
-  static_assert(NQ != 2 || NUM_SOFTMAX_WARPS * 32 * REG_SOFTMAX + 128 * REG_OTHER <=
+  static constexpr uint32_t REG_OTHER = CORR ? 72 : 120;
+  static constexpr uint32_t REG_CORR = 56;
+  static_assert(NQ != 2 || NUM_SOFTMAX_WARPS * 32 * REG_SOFTMAX + 128 * REG_OTHER +
+                                   (CORR ? 128 * REG_CORR : 0) <=
                                NUM_THREADS * LAUNCH_REGS,
                 "register split exceeds the launch allocation");
 
@@ -466,6 +501,9 @@ struct AttnConfig {
   // Arrivals per P part: one per softmax warp of the tile, of both CTAs for
   // pairs.
   static constexpr int P_ARRIVALS = WARPS_PER_TILE * CTAS;
+  // The first P part of a step also waits for the correction warps (O is
+  // rescaled, when it had to be, before P V adds to it).
+  static constexpr int P0_ARRIVALS = P_ARRIVALS + (CORR ? 4 : 0);
 };
 
 // Lazy-rescale threshold in log2 units: O and the row sum are rescaled only
@@ -951,7 +989,14 @@ __device__ __forceinline__ bool softmax_steps(int qi, uint32_t tmem, uint32_t sb
       m_run = mx;
       resc = true;
     }
-    if (__any_sync(0xffffffffu, resc)) {
+    if constexpr (C::CORR) {
+      // Hand this step's factor to the correction warpgroup, which rescales
+      // O where a row of this warp needs it before it lets P V add to O.
+      ptx::st_shared_f32(
+          sbase + C::OFF_CORR + 4u * ((qi * C::NSBUF + buf) * C::QROWS + wi * 32 + lane), alpha);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_CORR + qi * C::NSBUF + buf));
+    } else if (__any_sync(0xffffffffu, resc)) {
       // O holds the sum through PV(j-1); wait for that MMA, then scale in
       // place.  With one S buffer the S_FULL observed above already covers it.
       if constexpr (C::ODONE_PER_STEP) {
@@ -1065,6 +1110,17 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
   float m_run, l_run;
   bool ok = softmax_steps<T, C, PROFILE>(qi, tmem, sbase, p, w, prof, wt.kv_lo, wt.n, 0, wt.rank,
                                          m_run, l_run);
+  if constexpr (C::CORR) {
+    // The correction warpgroup normalises and stores O: hand it the row sums
+    // (after a failed wait the abort flag releases it instead).
+    if (ok) {
+      ptx::st_shared_f32(sbase + C::OFF_CORR + 4u * (C::CORR_ALPHA_FLOATS + qi * C::QROWS + row),
+                         l_run);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_CORR_END + qi));
+    }
+    return;
+  }
 
   // Epilogue: wait for the last P V, normalise, stage in the Q slot, TMA store.
   // Every warp of the group reaches both named barriers, also after a failed
@@ -1256,6 +1312,141 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
     }
     ptx::tma_store_wait_read0();
   }
+}
+
+// Correction warpgroup (AttnConfig::CORR; classic schedule, whole units).
+// Warp w serves rows 32 (w % 4) .. 32 (w % 4) + 31 of both Q tiles.
+//   Steps: for each step, tile 0 then tile 1, it takes the tile's rescale
+//   factors (BAR_CORR), rescales the rows of O that need it once P V of the
+//   previous step is complete, and adds its arrival to the first P part of
+//   the step, so the MMA warp issues P V only onto a rescaled O.  A step with
+//   no rescale costs it one wait and one arrival, off the softmax warps'
+//   path (the request comes after the row max, the first P part about a
+//   thousand cycles later).
+//   Epilogue: for each tile, the row sums (BAR_CORR_END) and the last P V
+//   (BAR_O_FINAL), then O / rowsum into the tile's Q slot (free once the
+//   last S has read it) in the TMA store's 128B-swizzled layout, and the TMA
+//   store.  Tile 0's runs while tile 1's last step does.
+// Every wait is bounded; after a failed one the abort flag releases the
+// other roles, and every correction warp still reaches each named barrier.
+template <typename T, class C>
+__device__ void correction_role(uint32_t tmem, uint32_t sbase, uint8_t* sgen,
+                                const CUtensorMap* tmO, const WorkTile& wt, const WaitCtx& w) {
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  const int wi = (threadIdx.x / 32) & 3;  // TMEM lane quarter
+  const int lane = threadIdx.x & 31;
+  const int row = wi * 32 + lane;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(wi * 32) << 16);
+  constexpr uint32_t kBarEpi = 3;  // named barrier of the correction warpgroup
+
+  // Step j of tile qi: rescale the rows of this warp that need it, then
+  // count in on the step's first P part.
+  auto step = [&](int qi, int j) -> bool {
+    const int buf = j % C::NSBUF;
+    const float alpha =
+        ptx::ld_shared_f32(sbase + C::OFF_CORR + 4u * ((qi * C::NSBUF + buf) * C::QROWS + row));
+    if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      // O holds the sum through P V of step j - 1 (j >= 1: the first step
+      // sets the max and never rescales).  With one S buffer S_i(j), whose
+      // completion the softmax has seen, was issued behind that P V by the
+      // same thread and committed after it; otherwise O_DONE says so.
+      bool done;
+      if constexpr (C::ODONE_PER_STEP) {
+        done = wait_bar(bar(C::BAR_O_DONE + qi), static_cast<uint32_t>((j - 1) & 1), w, kSiteODone);
+      } else {
+        done = wait_bar(bar(C::BAR_S_FULL + qi * C::NSBUF + buf),
+                        static_cast<uint32_t>((j / C::NSBUF) & 1), w, kSiteSFull);
+      }
+      if (!__all_sync(0xffffffffu, done)) return false;
+      ptx::tc_fence_after();
+      const uint32_t o_col = C::TMEM_O_COL + qi * C::D;
+#pragma unroll 1
+      for (int c = 0; c < C::D / 32; ++c) {
+        uint32_t o[32];
+        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+        ptx::tmem_st32(lane_base + o_col + c * 32, o);
+      }
+      ptx::tmem_wait_st();
+    }
+    ptx::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(bar(C::BAR_P_READY + (qi * C::NSBUF + buf) * C::PHALVES));
+    return true;
+  };
+
+  // Requests are served in step order, tile 0 then tile 1, with a bounded
+  // wait on the one expected next.  With one MMA issuer that is the order in
+  // which they come (S_0(j) completes before S_1(j)); with two, a tile that
+  // runs ahead waits at its first P part for the other's request of the same
+  // step.  (Serving whichever comes first by polling both barriers in turn
+  // measured far slower: a thread suspended in try_wait on one barrier woke
+  // up to ~2000 cycles after the other's request, which delayed P V.)  No
+  // request barrier runs two phases ahead (the request of step j + NSBUF
+  // needs the S that follows P V of step j).
+  bool ok = true;
+#pragma unroll 1
+  for (int j = 0; j < wt.n && ok; ++j) {
+    const uint32_t par = static_cast<uint32_t>((j / C::NSBUF) & 1);
+#pragma unroll 1
+    for (int qi = 0; qi < C::NQ && ok; ++qi) {
+      ok = __all_sync(0xffffffffu,
+                      wait_bar(bar(C::BAR_CORR + qi * C::NSBUF + j % C::NSBUF), par, w, kSiteCorr));
+      if (ok) ok = step(qi, j);
+    }
+  }
+
+#pragma unroll 1
+  for (int qi = 0; qi < C::NQ; ++qi) {
+    bool go = ok && *w.abort == 0;
+    if (go) go = wait_bar(bar(C::BAR_CORR_END + qi), 0, w, kSiteCorr);
+    if (go) go = wait_bar(bar(C::BAR_O_FINAL + qi), 0, w, kSiteODone);
+    go = __all_sync(0xffffffffu, go);
+    const uint32_t stage_s = sbase + C::OFF_Q + qi * C::Q_TILE_BYTES;
+    if (go) {
+      ptx::tc_fence_after();
+      const float inv =
+          1.f / ptx::ld_shared_f32(sbase + C::OFF_CORR +
+                                   4u * (C::CORR_ALPHA_FLOATS + qi * C::QROWS + row));
+      uint8_t* stage_g = sgen + C::OFF_Q + qi * C::Q_TILE_BYTES;
+      const uint32_t o_col = C::TMEM_O_COL + qi * C::D;
+#pragma unroll 1
+      for (int c = 0; c < C::D / 32; ++c) {
+        uint32_t o[32];
+        ptx::tmem_ld32(lane_base + o_col + c * 32, o);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(o);
+        // Columns 32c .. 32c + 31: four 16-byte chunks of 8 values each, in
+        // 64-column block (32c) / 64, chunk ((32c) % 64) / 8 + q, swizzled by
+        // the row (the layout of the TMA box {64, QROWS}).
+        const int dblk = (c * 32) / 64;
+        const int chunk0 = ((c * 32) % 64) / 8;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 u;
+          u.x = pack2<T>(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
+          u.y = pack2<T>(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
+          u.z = pack2<T>(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
+          u.w = pack2<T>(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
+          const int chunk = (chunk0 + q) ^ (row & 7);
+          *reinterpret_cast<uint4*>(stage_g + dblk * C::Q_BLK_BYTES + row * 128 + chunk * 16) = u;
+        }
+      }
+      ptx::fence_proxy_async_smem();
+    }
+    ptx::named_bar_sync(kBarEpi, 128);
+    if (wi == 0 && lane == 0 && *w.abort == 0) {
+#pragma unroll
+      for (int d = 0; d < C::DBLK; ++d)
+        ptx::tma_store_3d(tmO, stage_s + d * C::Q_BLK_BYTES, d * 64, wt.q_row0 + qi * C::QROWS,
+                          wt.bh);
+      ptx::tma_store_commit();
+    }
+  }
+  if (wi == 0 && lane == 0) ptx::tma_store_wait_read0();
 }
 
 // Profiler observer: stamps the completion of each P V of Q tile 0.  It only
@@ -1882,11 +2073,12 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase, u
 // PERSIST: the persistent schedule (AttnParams::grid and following), compiled as a
 // kernel of its own for the variants that have it (AttnConfig::PERSIST_OK),
 // so that its softmax loop and the classic one are allocated registers
-// separately.
+// separately.  CORR: the classic schedule with a correction warpgroup
+// (AttnConfig::CORR), whole units only.
 template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE, bool PAIR = false,
-          bool PERSIST = false>
-__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_THREADS,
-                                  AttnConfig<T, D, BN, NQ, STAGES, PAIR>::MIN_CTAS_PER_SM)
+          bool PERSIST = false, bool CORR = false>
+__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR>::NUM_THREADS,
+                                  AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR>::MIN_CTAS_PER_SM)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV,
@@ -1896,7 +2088,8 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_TH
 // generic compute_100 PTX (nvcc -arch=sm_100a does) gets an empty kernel there,
 // which a B200 never runs because the sm_100a binary matches it.
 #if defined(__CUDA_ARCH_FEAT_SM100_ALL) || !defined(__CUDA_ARCH__)
-  using C = AttnConfig<T, D, BN, NQ, STAGES, PAIR>;
+  using C = AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR>;
+  static_assert(!(CORR && PERSIST), "the correction warpgroup runs the classic schedule");
   constexpr int G = C::CTAS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = ptx::smem_u32(smem_raw);
@@ -1924,7 +2117,11 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_TH
     }
     for (int i = 0; i < C::NQ * C::NSBUF; ++i) ptx::mbar_init(bar(C::BAR_S_FULL + i), 1);
     for (int i = 0; i < C::NQ * C::NSBUF * C::PHALVES; ++i)
-      ptx::mbar_init(bar(C::BAR_P_READY + i), C::P_ARRIVALS);
+      ptx::mbar_init(bar(C::BAR_P_READY + i), i % C::PHALVES == 0 ? C::P0_ARRIVALS : C::P_ARRIVALS);
+    if constexpr (C::CORR) {
+      for (int i = 0; i < C::NQ * C::NSBUF + C::NQ; ++i)
+        ptx::mbar_init(bar(C::BAR_CORR + i), C::WARPS_PER_TILE);
+    }
     for (int i = 0; i < C::NQ; ++i) {
       ptx::mbar_init(bar(C::BAR_O_DONE + i), 1);
       ptx::mbar_init(bar(C::BAR_O_FINAL + i), 1);
@@ -1986,6 +2183,11 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR>::NUM_TH
   } else if (warp < C::NUM_SOFTMAX_WARPS) {
     if constexpr (C::NQ == 2) ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
     softmax_role<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, wt, p, w, prof);
+  } else if (C::CORR && warp >= C::CORR_WARP0) {
+    if constexpr (C::CORR) {
+      ptx::setmaxnreg_dec<C::REG_CORR>();
+      correction_role<T, C>(tmem, sbase, sgen, &tmO, wt, w);
+    }
   } else {
     if constexpr (C::NQ == 2) ptx::setmaxnreg_dec<C::REG_OTHER>();
     if (warp == C::LOAD_WARP) {

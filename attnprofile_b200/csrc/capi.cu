@@ -27,6 +27,7 @@ std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 std::atomic<int> g_fault_mode{0};
 std::atomic<int> g_split_mode{0};
 std::atomic<int> g_schedule_mode{0};
+std::atomic<int> g_corr_mode{0};
 constexpr int kMaxDev = 64;
 std::mutex g_status_mu;
 int* g_status_ptr[kMaxDev] = {};
@@ -75,6 +76,7 @@ static int run(const void* Q, const void* K, const void* V, void* O, int B, int 
   o.prof_cta = prof_cta;
   o.split = g_split_mode.load();
   o.schedule = g_schedule_mode.load();
+  o.corr = g_corr_mode.load() != 0;
   return dispatch(Q, K, V, O, B, H, S, D, SQO, SKV, dtype, BM, BN, st, o);
 }
 
@@ -114,6 +116,7 @@ int run_in_workspace(const void* Q, const void* K, const void* V, void* O, int B
   o.fault_mode = g_fault_mode.load();
   o.split = split_mode;
   o.schedule = g_schedule_mode.load();
+  o.corr = g_corr_mode.load() != 0;
   o.workspace = ws;
   o.workspace_bytes = ws_bytes;
   o.no_pool = true;
@@ -300,6 +303,12 @@ int attn_set_schedule(int mode) {
   return ATTN_OK;
 }
 
+int attn_set_correction(int mode) {
+  if (mode < 0 || mode > 1) return ATTN_ERR_INVALID_ARG;
+  g_corr_mode.store(mode);
+  return ATTN_OK;
+}
+
 int attn_plan_schedule(long long units, int num_kv_tiles, long long slots, int* persistent,
                        long long* ctas, int* pieces, double* persistent_cost_out,
                        double* classic_cost_out) {
@@ -336,6 +345,7 @@ int attn_query_split(int B, int H, int S, int D, int dtype, int BM, int BN, int*
   LaunchOpts o;
   o.split = g_split_mode.load();
   o.schedule = g_schedule_mode.load();
+  o.corr = g_corr_mode.load() != 0;
   o.plan_out = &pl;
   o.plan_only = true;
   const int rc = dispatch(nullptr, nullptr, nullptr, nullptr, B, H, S, D, S, S, dtype, BM, BN,

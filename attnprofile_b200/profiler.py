@@ -196,6 +196,8 @@ def main(argv=None):
                      help="also print N iterations (from 8) of one run's event timeline per tile")
     ap_.add_argument("--schedule", type=int, default=0, choices=[0, 1, 2],
                      help="attn_set_schedule mode (0 automatic, 1 classic, 2 persistent)")
+    ap_.add_argument("--correction", type=int, default=0, choices=[0, 1],
+                     help="attn_set_correction mode (1: correction warpgroup where built)")
     ap_.add_argument("--cta", type=int, default=None, help="CTA to profile (default: middle)")
     ap_.add_argument("--steps", action="store_true",
                      help="also print the per-step SOFTMAX starts of one run (item boundaries)")
@@ -204,6 +206,7 @@ def main(argv=None):
     a = ap_.parse_args(argv)
     import attnprofile_b200 as ap
     ap.set_schedule(a.schedule)
+    ap.set_correction(a.correction)
     print(f"B={a.b} H={a.h} S={a.s} D={a.d} {a.dtype}: cycles (clock64) per phase, "
           f"mean over KV iterations 0-31 and {a.runs} runs")
     print(table_header(a.epilogue))

@@ -73,6 +73,9 @@ def parse():
                     help="untimed back-to-back launches before timing (clock warm-up)")
     ap.add_argument("--schedule", type=int, default=0, choices=[0, 1, 2],
                     help="attn_set_schedule mode: 0 automatic (default), 1 classic, 2 persistent")
+    ap.add_argument("--correction", type=int, default=0, choices=[0, 1],
+                    help="attn_set_correction mode: 1 runs the tiles that have it with a "
+                         "correction warpgroup (default 0)")
     ap.add_argument("--no-sub", action="store_true",
                     help="skip the sub-records (C4/C5 strong scaling at every N, C3 at N=1)")
     a = ap.parse_args()
@@ -424,6 +427,7 @@ def main():
     ctx = Ctx()
     n, rank, dev = ctx.world, ctx.rank, ctx.dev
     ap.set_schedule(args.schedule)
+    ap.set_correction(args.correction)
     w = WORKLOADS[args.workload]
     cfg = config_of(args.workload, args, n)
     m = measure(ctx, args.workload, args.bm, args.bn, args.steps, args.warmup, args.preroll_s,
@@ -564,7 +568,8 @@ def main():
             "plan": dict(ap.query_split(cfg["B"], w["H"], S, D, BM=args.bm, BN=args.bn,
                                         dtype=0 if w["dtype"] == "f16" else 1),
                          schedule={0: "automatic (classic)", 1: "classic",
-                                   2: "persistent"}[args.schedule]),
+                                   2: "persistent"}[args.schedule],
+                         correction_warpgroup=bool(args.correction)),
         }
         line.update(subs)
         if gather is not None:

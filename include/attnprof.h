@@ -182,6 +182,20 @@ int attn_set_split(int mode);
  * (tuning/attn_test.cu:1583-1663).
  */
 int attn_set_schedule(int mode);
+
+/*
+ * attn_set_correction -- mode 1 runs launches made after this call with a
+ * correction warpgroup where the variant has one (BM = 256 with BN = 128,
+ * and BM = 256, BN = 96 at D = 64): a fourth warpgroup owns the lazy
+ * rescale of O in tensor memory (the softmax warps hand it each step's
+ * factors; it lets P V add to O only after rescaling), the final division by
+ * the row sums and the TMA store of O.  Such launches take the classic
+ * schedule without key split.  Mode 0 (default): the softmax warpgroups do
+ * that work themselves.  Same results either way.
+ * No counterpart in the reference, which rescales O eagerly inside its
+ * softmax consumer (tuning/attn_test.cu:305-321).
+ */
+int attn_set_correction(int mode);
 int attn_plan_schedule(long long units, int num_kv_tiles, long long slots, int* persistent,
                        long long* ctas, int* pieces, double* persistent_cost,
                        double* classic_cost);
