@@ -429,7 +429,11 @@ struct AttnConfig {
   // on the per-tile chain.  K_{j+1}'s own FULL barrier still gets one plain
   // arrival from the producer, so every slot's barrier advances one phase per
   // item and the phase parities stay (t / STAGES) & 1.
-  static constexpr bool KV_JOINT_FULL = kJointFull && V_RELEASE_WITH_K && !PAIR;
+  //
+  // Pairs too: the odd CTA's loads land on its own barriers, which the relay
+  // forwards to the even CTA's; under the joint landing the relay forwards
+  // K_{j+1}'s slot before V_j's (see relay_role).
+  static constexpr bool KV_JOINT_FULL = kJointFull && V_RELEASE_WITH_K;
   static constexpr int K_SLOT_PERIOD = STAGES % 2 == 0 ? STAGES / 2 : STAGES;
   static constexpr int BAR_O_FINAL = BAR_O_DONE + NQ;            // the last P V of tile i
   static constexpr int BAR_DRAIN = BAR_O_FINAL + NQ;
@@ -877,11 +881,38 @@ __device__ void relay_role(uint32_t sbase, const WorkTile& wt, const WaitCtx& w)
     if (!wait(bar(C::BAR_Q + i), 0, kSiteQ)) return;
     ptx::mbar_arrive_cluster(ptx::mapa_shared(bar(C::BAR_Q + i), 0));
   }
-  const int items = 2 * wt.n;
-  for (int t = 0; t < items; ++t) {
-    const int s = t % C::STAGES;
-    if (!wait(bar(C::BAR_KV_FULL + s), (t / C::STAGES) & 1, kSiteKvFull)) return;
-    ptx::mbar_arrive_cluster(ptx::mapa_shared(bar(C::BAR_KV_FULL + s), 0));
+  auto wait_item = [&](int t) {
+    return wait(bar(C::BAR_KV_FULL + t % C::STAGES), (t / C::STAGES) & 1, kSiteKvFull);
+  };
+  auto forward = [&](int t) {
+    ptx::mbar_arrive_cluster(ptx::mapa_shared(bar(C::BAR_KV_FULL + t % C::STAGES), 0));
+  };
+  if constexpr (C::KV_JOINT_FULL) {
+    // Items K_0, then V_j (t = 2j + 1) and K_{j+1} (t = 2j + 2).  V_j's
+    // barrier here completes only after K_{j+1}'s loads land (they were
+    // issued after K's plain arrival), so once it has, K's phase is complete
+    // too, and neither can move on before the even CTA's issuer sees V_j
+    // forwarded.  K's slot is forwarded first: the even CTA's K barrier then
+    // completes this phase before its producer, which waits for the commit
+    // that follows V_j, can arrive for the slot's next item.
+    static_assert(C::NSBUF == 1, "the joint landing interleaves one K per V");
+    if (!wait_item(0)) return;
+    forward(0);
+    for (int j = 0; j < wt.n; ++j) {
+      const int tv = 2 * j + 1;
+      if (!wait_item(tv)) return;
+      if (j + 1 < wt.n) {
+        if (!wait_item(tv + 1)) return;
+        forward(tv + 1);
+      }
+      forward(tv);
+    }
+  } else {
+    const int items = 2 * wt.n;
+    for (int t = 0; t < items; ++t) {
+      if (!wait_item(t)) return;
+      forward(t);
+    }
   }
 }
 
