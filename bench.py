@@ -136,16 +136,64 @@ def config_of(wl, args, n):
 # clocks sampler (nvidia-smi during the timed region)
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock, its maximum, board power and the throttle reasons of one GPU,
+    sampled while a region runs: through NVML in a thread every 5 ms (so a
+    region of a few ms still gets samples), else an `nvidia-smi -lms 100`
+    loop.  It only reads the GPU's state."""
     Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    PERIOD_S = 0.005
 
     def __init__(self, device_index):
         self.dev = device_index
         self.proc = None
         self.lines = []
+        self.samples = []  # NVML: (sm MHz, max MHz, watts or None, set of reasons)
+        self.nvml = None
+        self.stop_ev = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            get = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.get_reasons = get
+            self.bits = [0x8, 0x40, 0x20, 0x4]  # NVML's bits for NAMES
+        except Exception:
+            self.nvml = None
+
+    def _sample_nvml(self):
+        nv = self.nvml
+        sm = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+        try:
+            watts = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+        except Exception:
+            watts = None
+        try:
+            r = int(self.get_reasons(self.h))
+            reasons = {nm for nm, b in zip(self.NAMES, self.bits) if r & b}
+        except Exception:
+            reasons = set()
+        self.samples.append((sm, self.max_mhz, watts, reasons))
+
+    def _loop_nvml(self):
+        while not self.stop_ev.is_set():
+            try:
+                self._sample_nvml()
+            except Exception:
+                return
+            self.stop_ev.wait(self.PERIOD_S)
 
     def start(self):
+        if self.nvml is not None:
+            self.stop_ev.clear()
+            self.t = threading.Thread(target=self._loop_nvml, daemon=True)
+            self.t.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
@@ -160,38 +208,56 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def mark(self):
+        """The timed region starts now: the summary keeps the samples from
+        here on and the one just before (the sampler runs from before the
+        pre-roll so that it is up when the region starts)."""
+        self.mark_at = max(0, (len(self.samples) if self.nvml is not None else len(self.lines)) - 1)
+
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.t.join(timeout=2)
-        sm, mx, pw, reasons = [], [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 7:
-                continue
+        if self.nvml is not None:
+            self.stop_ev.set()
+            self.t.join(timeout=2)
             try:
-                sm.append(float(parts[0]))
-                mx.append(float(parts[1]))
-            except ValueError:
-                continue
-            try:
-                pw.append(float(parts[2]))
-            except ValueError:
+                self._sample_nvml()  # the state at the end of the region
+            except Exception:
                 pass
-            for nm, val in zip(names, parts[3:7]):
-                if val.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
+            rows = list(self.samples[getattr(self, "mark_at", 0):])
+            self.samples = []
+        elif self.proc is None:
+            return None
+        else:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.t.join(timeout=2)
+            rows = []
+            for ln in self.lines[getattr(self, "mark_at", 0):]:
+                parts = [x.strip() for x in ln.split(",")]
+                if len(parts) < 7:
+                    continue
+                try:
+                    sm, mx = float(parts[0]), float(parts[1])
+                except ValueError:
+                    continue
+                try:
+                    pw = float(parts[2])
+                except ValueError:
+                    pw = None
+                rows.append((sm, mx, pw, {nm for nm, val in zip(self.NAMES, parts[3:7])
+                                          if val.lower() == "active"}))
+            self.lines = []
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm),
-                "power_w": statistics.median(pw) if pw else None}
+        pw = [r[2] for r in rows if r[2] is not None]
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows),
+                "sm_mhz_min": min(r[0] for r in rows),
+                "reasons": sorted(set().union(*(r[3] for r in rows))), "samples": len(rows),
+                "power_w": statistics.median(pw) if pw else None,
+                "how": "NVML every 5 ms" if self.nvml is not None else "nvidia-smi -lms 100"}
 
 
 # ---------------------------------------------------------------------------
@@ -347,6 +413,13 @@ def measure(ctx, wl, bm, bn, steps, warmup, preroll_s, seed, keep_sets=False):
     if rc != 0:
         raise SystemExit(f"{wl}: device status after warm-up: {rc} site {site:#x}")
 
+    # A first barrier before the pre-roll: it also sets up the collectives
+    # (NCCL creates its communicator on the first one, which can idle the
+    # GPUs long enough for their clocks to drop), so the barrier right before
+    # timing is a short one and the pre-roll runs directly ahead of the
+    # timed steps.
+    ctx.barrier()
+    torch.cuda.synchronize()
     sampler = ClockSampler(ctx.local)
     sampler.start()
     t_end = time.perf_counter() + preroll_s
@@ -362,6 +435,7 @@ def measure(ctx, wl, bm, bn, steps, warmup, preroll_s, seed, keep_sets=False):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx.barrier()
     torch.cuda.synchronize()
+    sampler.mark()
     ev0.record(stream)
     for i in range(steps):
         launch(i)
