@@ -564,7 +564,9 @@ __global__ void __launch_bounds__(288, 1) issue_probe(unsigned long long* stamps
 // MMAs of 128 x 64 x 16 (32 cycles of work) into their own accumulators, in
 // a rolled loop.  If the cost of an issue is per thread, two issuers come
 // closer to the math rate; if it is per SM, they do not.
-template <int ISSUERS>
+// ELECT: the issuing warp runs the loop with all 32 lanes and elect.sync
+// picks the lane that issues each MMA and the commit.
+template <int ISSUERS, bool ELECT = false>
 __global__ void __launch_bounds__(128, 1) issue_rate_probe(int n, unsigned long long* cycles) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -587,7 +589,19 @@ __global__ void __launch_bounds__(128, 1) issue_rate_probe(int n, unsigned long 
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  if (warp < ISSUERS && lane == 0) {
+  if (ELECT && warp < ISSUERS) {
+    const uint32_t id = ptx::idesc_f16(128, 64, false, false);
+    const uint64_t qd = ptx::smem_desc_sw128(base, 16, 1024);
+    const uint64_t kd = ptx::smem_desc_sw128(base + 32768, 16, 1024);
+    __syncwarp();
+    const unsigned long long t0 = clock64();
+#pragma unroll 1
+    for (int i = 0; i < n; ++i) ptx::mma_ss_elect(tmem + warp * 256 + (i & 1) * 64, qd, kd, id, 0u);
+    ptx::mma_commit_elect(ptx::smem_u32(&done[warp]));
+    bounded_wait(ptx::smem_u32(&done[warp]), 0);
+    __syncwarp();
+    if (lane == 0) cycles[blockIdx.x * 2 + warp] = clock64() - t0;
+  } else if (!ELECT && warp < ISSUERS && lane == 0) {
     const uint32_t id = ptx::idesc_f16(128, 64, false, false);
     const uint64_t qd = ptx::smem_desc_sw128(base, 16, 1024);
     const uint64_t kd = ptx::smem_desc_sw128(base + 32768, 16, 1024);
@@ -772,19 +786,23 @@ int main(int argc, char** argv) {
     cudaFree(st);
 
     const int total = 512;  // MMAs of 128 x 64 x 16 per CTA, 32 cycles of work each
-    double c[2];
-    for (int k = 0; k < 2; ++k) {
-      auto kern = k == 0 ? issue_rate_probe<1> : issue_rate_probe<2>;
+    double c[4];
+    for (int k = 0; k < 4; ++k) {
+      auto kern = k == 0 ? issue_rate_probe<1> : k == 1 ? issue_rate_probe<2>
+                : k == 2 ? issue_rate_probe<1, true> : issue_rate_probe<2, true>;
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_SMEM);
       cudaMemset(cyc, 0, sizeof(unsigned long long) * 3 * sms);
-      for (int rep = 0; rep < 2; ++rep) kern<<<sms, 128, MMA_SMEM>>>(total / (k + 1), cyc);
+      const int issuers = k % 2 + 1;
+      for (int rep = 0; rep < 2; ++rep) kern<<<sms, 128, MMA_SMEM>>>(total / issuers, cyc);
       if (!check("issue")) return 1;
       cudaMemcpy(h.data(), cyc, sizeof(unsigned long long) * 2 * sms, cudaMemcpyDeviceToHost);
-      c[k] = k == 0 ? mean_of(h, 2, 0, sms) : std::max(mean_of(h, 2, 0, sms), mean_of(h, 2, 1, sms));
+      c[k] = issuers == 1 ? mean_of(h, 2, 0, sms)
+                          : std::max(mean_of(h, 2, 0, sms), mean_of(h, 2, 1, sms));
     }
     std::printf("issue    %d MMAs of 128x64x16 (32 cycles of work each, rolled loop): one issuing "
-                "thread %.1f cycles / MMA, two issuing threads %.1f\n", total, c[0] / total,
-                c[1] / total);
+                "thread %.1f cycles / MMA, two issuing threads %.1f; issued from whole warps "
+                "through elect.sync: one warp %.1f, two warps %.1f\n", total, c[0] / total,
+                c[1] / total, c[2] / total, c[3] / total);
   }
   cudaFree(cyc);
   cudaFree(sink);
