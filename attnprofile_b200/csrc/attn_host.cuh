@@ -430,8 +430,9 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   // unit per cluster; pairs take no key split).
   const long long qt = (S + C::BM * C::CTAS - 1) / (C::BM * C::CTAS);
   const int n_kv = (S + BN - 1) / BN;
-  // (The correction-warpgroup kernel stores whole units only: no key split.)
-  SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, (PAIR || corr) ? 1 : o.split);
+  // (The correction-warpgroup kernel and the eight-warp tiles store whole
+  // units only: no key split.)
+  SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, (PAIR || corr || C::W8) ? 1 : o.split);
   plan_workspace(&plan, C::BM, D, NQ, sizeof(float));
   // Persistent schedule: only when asked for (attn_set_schedule(2)), where
   // the variant has it and the split mode is automatic.  The automatic mode

@@ -296,6 +296,12 @@ constexpr int kPsplitQuarters = ATTNPROF_PSPLIT_QUARTERS;
 #define ATTNPROF_LEAN_COMMITS 1
 #endif
 constexpr bool kLeanCommits = ATTNPROF_LEAN_COMMITS != 0;
+// 1 (default): the double-buffered D = 64 tiles run eight softmax warps per Q
+// tile, 16 rows each (AttnConfig::W8); 0: four, 32 rows each.
+#ifndef ATTNPROF_W8
+#define ATTNPROF_W8 1
+#endif
+constexpr bool kW8 = ATTNPROF_W8 != 0;
 // 1 (default): one FULL wait per step for V_j and K_{j+1} (AttnConfig::KV_JOINT_FULL).
 #ifndef ATTNPROF_JOINT_FULL
 #define ATTNPROF_JOINT_FULL 1
@@ -393,11 +399,19 @@ struct AttnConfig {
   // the softmax computes the rest: with >= 2 chunks of 32 columns, part 0 is
   // the first PSPLIT_CHUNKS chunks (P V K-steps [0, 2 * PSPLIT_CHUNKS)).
   // Variants that double-buffer S at D = 64 keep both softmax warpgroups on
-  // the exponentials back to back, where the MUFU unit is the bound: there a
-  // quarter of the exponentials go to the FMA pipe and P is published in one
-  // piece (C3 at 256 x 96: 631 -> 664 TFLOP/s).  At D = 128 neither helps.
+  // the exponentials back to back, where the MUFU unit is the bound: there
+  // part of the exponentials go to the FMA pipe (POLY8) and P is published in
+  // one piece (C3 at 256 x 96: 631 -> 664 TFLOP/s).  At D = 128 neither helps.
   static constexpr bool EXP_BOUND = NQ == 2 && D == 64 && NQ * (2 * BN + D) <= 512;
   static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND) ? 2 : 1;
+  // W8: those tiles give each Q tile eight softmax warps of 16 rows (the
+  // 16-lane tensor-memory forms), so that four softmax warps share each SM
+  // sub-partition and its exponential unit instead of two: their softmax
+  // step is bound by the exponentials and by each warp's own instruction
+  // stream.  (At D = 128 the single issuer's chain makes a step's latency
+  // matter, and eight warps per tile measured slower there.)  Whole units
+  // only: such launches take no key split.
+  static constexpr bool W8 = kW8 && EXP_BOUND && !PAIR && !CORR;
   static constexpr int PSPLIT_QUARTERS = kPsplitQuarters >= 0 ? kPsplitQuarters
                                                               : (BN == 128 ? 3 : 2);
   static constexpr int PSPLIT_CHUNKS =
@@ -460,7 +474,7 @@ struct AttnConfig {
   static constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for manual 1024 B alignment
 
   // Warp roles.
-  static constexpr int WARPS_PER_TILE = 4;
+  static constexpr int WARPS_PER_TILE = W8 ? 8 : 4;
   static constexpr int NUM_SOFTMAX_WARPS = WARPS_PER_TILE * NQ;
   static constexpr int LOAD_WARP = NUM_SOFTMAX_WARPS;
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;
@@ -490,15 +504,21 @@ struct AttnConfig {
   // 2 x 128 x 192 + producer/MMA 128 x 72 + correction 128 x 56 (the MMA
   // issuer spills below 72).
   static constexpr int LAUNCH_REGS = (65536 / NUM_THREADS) & ~7;
-  static constexpr uint32_t REG_SOFTMAX = 192;
-  static constexpr uint32_t REG_OTHER = CORR ? 72 : 120;
+  // W8: 640 threads launched at 96 (61440): softmax 16 x 32 x 104 + the
+  // producer/MMA warpgroup 128 x 64.
+  static constexpr uint32_t REG_SOFTMAX = W8 ? 104 : 192;
+  static constexpr uint32_t REG_OTHER = W8 ? 64 : (CORR ? 72 : 120);
   static constexpr uint32_t REG_CORR = 56;
   static_assert(NQ != 2 || NUM_SOFTMAX_WARPS * 32 * REG_SOFTMAX + 128 * REG_OTHER +
                                    (CORR ? 128 * REG_CORR : 0) <=
                                NUM_THREADS * LAUNCH_REGS,
                 "register split exceeds the launch allocation");
 
-  static constexpr int POLY8 = kPolyPairsOf8 >= 0 ? kPolyPairsOf8 : (EXP_BOUND ? 2 : 0);
+  // Polynomial share: 2 of 8 pairs on the four-warp EXP_BOUND tiles, 1 of 8
+  // with eight warps per tile (C3: 709-711 TFLOP/s against 693-695 at 2 and
+  // 696 at 0), none elsewhere.
+  static constexpr int POLY8 =
+      kPolyPairsOf8 >= 0 ? kPolyPairsOf8 : (W8 ? 1 : (EXP_BOUND ? 2 : 0));
   static constexpr int MMA_M = 128 * CTAS;
   static constexpr uint32_t IDESC_S = ptx::idesc_f16(MMA_M, BN, kBF16, false);
   static constexpr uint32_t IDESC_PV = ptx::idesc_f16(MMA_M, D, kBF16, true);
@@ -1341,6 +1361,251 @@ __device__ void softmax_role(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sge
       prof.stamp(kPhEpilogue, kEpStore, 1);
       prof.stamp(kPhEpilogue, kEpAll, 1);
     }
+    ptx::tma_store_wait_read0();
+  }
+}
+
+// Eight softmax warps per Q tile (AttnConfig::W8; two S buffers, P in one
+// part, whole units).  Warp w of tile i serves TMEM lanes 32 (w % 4) +
+// 16 ((w / 4) % 2) .. + 15 through the 16-lane forms: thread t holds rows
+// r = 16-lane base + t / 4 and r + 8, and per 8-key block the two keys
+// 2 (t % 4), 2 (t % 4) + 1 of each.  The four threads of a row combine its
+// maximum by two shuffles; its sum stays a per-thread partial (rescaled by
+// the same factors) until the epilogue adds the four.  The arithmetic per
+// element is the four-warp step's: same argument FMA, exponential and
+// rounding of P; the row max is the same value; the row sum is added up in
+// another order.
+template <int NB>
+__device__ __forceinline__ void tmem_ld_rows16(uint32_t taddr, uint32_t (&r)[4 * NB]) {
+  static_assert(NB % 4 == 0, "8-column blocks in multiples of 4");
+#pragma unroll
+  for (int k = 0; k + 8 <= NB; k += 8)
+    ptx::tmem_ld16x256b_x8(taddr + 8 * k, *reinterpret_cast<uint32_t(*)[32]>(&r[4 * k]));
+  if constexpr (NB % 8 == 4)
+    ptx::tmem_ld16x256b_x4(taddr + 8 * (NB - 4), *reinterpret_cast<uint32_t(*)[16]>(&r[4 * (NB - 4)]));
+}
+
+template <int NB>
+__device__ __forceinline__ void tmem_st_rows16(uint32_t taddr, const uint32_t (&r)[4 * NB]) {
+#pragma unroll
+  for (int k = 0; k + 8 <= NB; k += 8)
+    ptx::tmem_st16x256b_x8(taddr + 8 * k, *reinterpret_cast<const uint32_t(*)[32]>(&r[4 * k]));
+  if constexpr (NB % 8 == 4)
+    ptx::tmem_st16x256b_x4(taddr + 8 * (NB - 4),
+                           *reinterpret_cast<const uint32_t(*)[16]>(&r[4 * (NB - 4)]));
+}
+
+// P of NB 8-key blocks: 4 NB packed columns, two registers per 4 columns.
+template <int NB>
+__device__ __forceinline__ void tmem_st_p16(uint32_t taddr, const uint32_t (&pk)[2 * NB]) {
+#pragma unroll
+  for (int k = 0; k + 8 <= NB; k += 8)
+    ptx::tmem_st16x128b_x8(taddr + 4 * k, *reinterpret_cast<const uint32_t(*)[16]>(&pk[2 * k]));
+  if constexpr (NB % 8 == 4)
+    ptx::tmem_st16x128b_x4(taddr + 4 * (NB - 4),
+                           *reinterpret_cast<const uint32_t(*)[8]>(&pk[2 * (NB - 4)]));
+}
+
+template <typename T, class C, bool PROFILE>
+__device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sgen,
+                               const CUtensorMap* tmO, const WorkTile& wt, const AttnParams& p,
+                               const WaitCtx& w, const Prof<PROFILE>& prof) {
+  static_assert(C::NSBUF == 2 && C::PHALVES == 1 && !C::PAIR, "W8 serves two-buffer tiles");
+  static_assert(C::BN % 32 == 0 && C::D % 32 == 0, "");
+  constexpr int NB = C::BN / 8;  // 8-key blocks of S
+  constexpr int NO = C::D / 8;   // 8-column blocks of O
+  auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int row0 = 32 * (warp & 3) + 16 * ((warp >> 2) & 1);  // first TMEM lane of this warp
+  const int rA = row0 + lane / 4, rB = rA + 8;                 // this thread's rows
+  const int kc = 2 * (lane & 3);                               // its first key of each block
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(row0) << 16);
+  const uint32_t o_col = C::TMEM_O_COL + qi * C::D;
+  const float sl2 = p.scale_log2;
+  const bool lead = row0 == 0 && lane == 0;
+  const bool rec = PROFILE && qi == 0 && lead;
+  const bool rec1 = PROFILE && qi == 1 && lead;
+  const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
+
+  float mA = -INFINITY, mB = -INFINITY;  // running maxima of rows rA, rB
+  float lA = 0.f, lB = 0.f;              // this thread's partial row sums
+  bool ok = true;
+  for (int j = 0; j < wt.n; ++j) {
+    const int sl = j < kProfSlots ? j : kProfSlots;
+    const int buf = j % C::NSBUF;
+    const uint32_t s_col = (qi * C::NSBUF + buf) * C::BN;
+    ok = __all_sync(0xffffffffu, wait_bar(bar(C::BAR_S_FULL + qi * C::NSBUF + buf),
+                                          static_cast<uint32_t>((j / C::NSBUF) & 1), w, kSiteSFull));
+    if (!ok) break;
+    ptx::tc_fence_after();
+    if (rec) {
+      prof.stamp(kPhQK, sl, 1);
+      prof.stamp(kPhSoftmax, sl, 0);
+      prof.stamp(kPhSmLoadS, sl, 0);
+    }
+    if (rec1) prof.stamp(kPhSoftmaxT1, sl, 0);
+    uint32_t sr[4 * NB];
+    tmem_ld_rows16<NB>(lane_base + s_col, sr);
+    ptx::tmem_wait_ld();
+    ptx::reg_fence(sr);
+    if (rec) {
+      prof.stamp(kPhSmLoadS, sl, 1);
+      prof.stamp(kPhSmMax, sl, 0);
+    }
+    const int lim = p.S - (wt.kv_lo + j) * C::BN;  // valid keys in this tile
+    if (lim < C::BN) {
+#pragma unroll
+      for (int k = 0; k < NB; ++k)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (8 * k + kc + (e & 1) >= lim) sr[4 * k + e] = __float_as_uint(-INFINITY);
+    }
+    float xa[2] = {-INFINITY, -INFINITY}, xb[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      xa[k & 1] = ptx::fmax3(xa[k & 1], __uint_as_float(sr[4 * k]), __uint_as_float(sr[4 * k + 1]));
+      xb[k & 1] = ptx::fmax3(xb[k & 1], __uint_as_float(sr[4 * k + 2]), __uint_as_float(sr[4 * k + 3]));
+    }
+    float xA = fmaxf(xa[0], xa[1]), xB = fmaxf(xb[0], xb[1]);
+    xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 1));
+    xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 1));
+    xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 2));
+    xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 2));
+
+    // Lazy rescale per row, as in the four-warp step.
+    float aA = 1.f, aB = 1.f;
+    bool resc = false;
+    if (j == 0) {
+      mA = xA;
+      mB = xB;
+    } else {
+      if ((xA - mA) * sl2 > RESCALE_THRESHOLD) {
+        aA = ptx::ex2_approx((mA - xA) * sl2);
+        mA = xA;
+        resc = true;
+      }
+      if ((xB - mB) * sl2 > RESCALE_THRESHOLD) {
+        aB = ptx::ex2_approx((mB - xB) * sl2);
+        mB = xB;
+        resc = true;
+      }
+    }
+    if (__any_sync(0xffffffffu, resc)) {
+      // O holds the sum through P V of step j - 1: wait for it (two S
+      // buffers commit O_DONE every step), then scale in place.
+      ok = __all_sync(0xffffffffu, wait_bar(bar(C::BAR_O_DONE + qi),
+                                            static_cast<uint32_t>((j - 1) & 1), w, kSiteODone));
+      if (!ok) break;
+      ptx::tc_fence_after();
+      uint32_t o[4 * NO];
+      tmem_ld_rows16<NO>(lane_base + o_col, o);
+      ptx::tmem_wait_ld();
+      ptx::reg_fence(o);
+#pragma unroll
+      for (int k = 0; k < NO; ++k) {
+        o[4 * k] = __float_as_uint(__uint_as_float(o[4 * k]) * aA);
+        o[4 * k + 1] = __float_as_uint(__uint_as_float(o[4 * k + 1]) * aA);
+        o[4 * k + 2] = __float_as_uint(__uint_as_float(o[4 * k + 2]) * aB);
+        o[4 * k + 3] = __float_as_uint(__uint_as_float(o[4 * k + 3]) * aB);
+      }
+      tmem_st_rows16<NO>(lane_base + o_col, o);
+    }
+    if (rec) {
+      prof.stamp(kPhSmMax, sl, 1);
+      prof.stamp(kPhSmExp, sl, 0);
+    }
+
+    // P = exp2(s * scale_log2 - m * scale_log2), rounded to T, over S.
+    const float negA = -mA * sl2, negB = -mB * sl2;
+    const uint64_t negA2 = ptx::f2_pack(negA, negA), negB2 = ptx::f2_pack(negB, negB);
+    const float poly_a = sl2 * (1.0f / 134.0f);
+    const float poly_bA = (negA + 126.0f) * (1.0f / 134.0f);
+    const float poly_bB = (negB + 126.0f) * (1.0f / 134.0f);
+    uint64_t sumA2 = 0ull, sumB2 = 0ull;
+    uint32_t pk[2 * NB];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float s0 = __uint_as_float(sr[4 * k + 2 * r]), s1 = __uint_as_float(sr[4 * k + 2 * r + 1]);
+        float p0, p1;
+        if (poly_pair<C::POLY8>((2 * k + r) % 16)) {
+          ptx::exp2_poly_pair(s0, s1, poly_a, r ? poly_bB : poly_bA, p0, p1);
+        } else {
+          const uint64_t x2 = ptx::f2_fma(ptx::f2_pack(s0, s1), sl2x2, r ? negB2 : negA2);
+          float x0, x1;
+          ptx::f2_unpack(x2, x0, x1);
+          p0 = ptx::ex2_approx(x0);
+          p1 = ptx::ex2_approx(x1);
+        }
+        if (r)
+          sumB2 = ptx::f2_add(sumB2, ptx::f2_pack(p0, p1));
+        else
+          sumA2 = ptx::f2_add(sumA2, ptx::f2_pack(p0, p1));
+        pk[2 * k + r] = pack2<T>(p0, p1);
+      }
+    }
+    tmem_st_p16<NB>(lane_base + s_col, pk);
+    float s0, s1, s2, s3;
+    ptx::f2_unpack(sumA2, s0, s1);
+    ptx::f2_unpack(sumB2, s2, s3);
+    if (rec) {
+      prof.stamp(kPhSmExp, sl, 1);
+      prof.stamp(kPhSmStoreP, sl, 0);
+    }
+    ptx::tmem_wait_st();
+    if (rec) prof.stamp(kPhSmStoreP, sl, 1);
+    ptx::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(bar(C::BAR_P_READY + (qi * C::NSBUF + buf) * C::PHALVES));
+    if (rec) prof.stamp(kPhSoftmax, sl, 1);
+    if (rec1) prof.stamp(kPhSoftmaxT1, sl, 1);
+    lA = lA * aA + (s0 + s1);
+    lB = lB * aB + (s2 + s3);
+  }
+
+  // Epilogue: the row sums, then O / rowsum into the Q slot and a TMA store.
+  lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+  lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+  constexpr uint32_t kTileThreads = 32 * C::WARPS_PER_TILE;
+  if (rec) prof.stamp(kPhEpilogue, kEpAll, 0);
+  ptx::named_bar_sync(1 + qi, kTileThreads);
+  bool go = ok && (*w.abort == 0);
+  if (go) go = wait_bar(bar(C::BAR_O_FINAL + qi), 0, w, kSiteODone);
+  go = __all_sync(0xffffffffu, go);
+  const uint32_t stage_s = sbase + C::OFF_Q + qi * C::Q_TILE_BYTES;
+  uint8_t* stage_g = sgen + C::OFF_Q + qi * C::Q_TILE_BYTES;
+  if (go) {
+    ptx::tc_fence_after();
+    const float invA = 1.f / lA, invB = 1.f / lB;
+    uint32_t o[4 * NO];
+    tmem_ld_rows16<NO>(lane_base + o_col, o);
+    ptx::tmem_wait_ld();
+    ptx::reg_fence(o);
+    // Columns 8k + kc, + 1 of rows rA and rB: one 4-byte value each in the
+    // 128B-swizzled staging tile (the TMA box {64, QROWS}).
+#pragma unroll
+    for (int k = 0; k < NO; ++k) {
+      const int dblk = (8 * k) / 64, chunk = ((8 * k) % 64) / 8;
+      const uint32_t va = pack2<T>(__uint_as_float(o[4 * k]) * invA, __uint_as_float(o[4 * k + 1]) * invA);
+      const uint32_t vb = pack2<T>(__uint_as_float(o[4 * k + 2]) * invB, __uint_as_float(o[4 * k + 3]) * invB);
+      *reinterpret_cast<uint32_t*>(stage_g + dblk * C::Q_BLK_BYTES + rA * 128 +
+                                   ((chunk ^ (rA & 7)) * 16) + 2 * kc) = va;
+      *reinterpret_cast<uint32_t*>(stage_g + dblk * C::Q_BLK_BYTES + rB * 128 +
+                                   ((chunk ^ (rB & 7)) * 16) + 2 * kc) = vb;
+    }
+    ptx::fence_proxy_async_smem();
+  }
+  ptx::named_bar_sync(1 + qi, kTileThreads);
+  if (lead && *w.abort == 0) {
+#pragma unroll
+    for (int d = 0; d < C::DBLK; ++d)
+      ptx::tma_store_3d(tmO, stage_s + d * C::Q_BLK_BYTES, d * 64, wt.q_row0 + qi * C::QROWS, wt.bh);
+    ptx::tma_store_commit();
+    if (rec) prof.stamp(kPhEpilogue, kEpAll, 1);
     ptx::tma_store_wait_read0();
   }
 }
@@ -2213,7 +2478,11 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR>::
     }
   } else if (warp < C::NUM_SOFTMAX_WARPS) {
     if constexpr (C::NQ == 2) ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
-    softmax_role<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, wt, p, w, prof);
+    if constexpr (C::W8)
+      softmax_role16<T, C, PROFILE>(warp / C::WARPS_PER_TILE, tmem, sbase, sgen, &tmO, wt, p, w,
+                                    prof);
+    else
+      softmax_role<T, C, PROFILE>(warp / 4, tmem, sbase, sgen, &tmO, wt, p, w, prof);
   } else if (C::CORR && warp >= C::CORR_WARP0) {
     if constexpr (C::CORR) {
       ptx::setmaxnreg_dec<C::REG_CORR>();
