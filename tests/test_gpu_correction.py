@@ -27,6 +27,14 @@ def _restore(engine):
     engine.set_split(0)
 
 
+def same_softmax(D, BN):
+    """Does the default kernel run the same softmax as the correction-
+    warpgroup kernel on this tile?  Not on the D = 64 tiles with two S
+    buffers (256 x 96 here): there the default has eight softmax warps per Q
+    tile and another polynomial share, so its bits may differ."""
+    return not (D == 64 and 2 * (2 * BN + D) <= 512)
+
+
 def run(engine, q, k, v, BM, BN, corr):
     torch = _torch()
     engine.set_correction(corr)
@@ -69,8 +77,9 @@ def test_correction_moving_row_max(engine, oracle_mod, D, BN, ramp):
     """Keys scaled by a ramp over the sequence: 'up' makes the row max grow by
     far more than the lazy-rescale threshold from tile to tile, so the
     correction warps rescale O on most steps; 'down' puts the max in the
-    first tile (no rescale after it).  The result must equal the classic
-    kernel's bit for bit and the oracle's within the bounds.  V is N(0, 0.5^2):
+    first tile (no rescale after it).  The result must equal the default
+    kernel's bit for bit where both run the same softmax, and the oracle's
+    within the bounds.  V is N(0, 0.5^2):
     with attention this concentrated, O is close to single rows of V, and an
     f16 output at |O| >= 4 has an ulp (3.9e-3) above the 2e-3 bound, so one
     rounding step there would decide the test rather than the kernel."""
@@ -83,7 +92,8 @@ def test_correction_moving_row_max(engine, oracle_mod, D, BN, ramp):
     engine.set_split(1)
     classic = run(engine, q, k, v, 256, BN, 0)
     out = run(engine, q, k, v, 256, BN, 1)
-    assert torch.equal(out, classic), (out.float() - classic.float()).abs().max().item()
+    if same_softmax(D, BN):
+        assert torch.equal(out, classic), (out.float() - classic.float()).abs().max().item()
     ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
     mx, mean = compare(oracle_mod, to_u16(out), ref, 0)
     assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
@@ -91,14 +101,16 @@ def test_correction_moving_row_max(engine, oracle_mod, D, BN, ramp):
 
 @pytest.mark.parametrize("B,H,S,D,BN,ramp", [
     (1, 16, 4096, 128, 128, False),
-    (1, 16, 4096, 64, 96, False),
+    (1, 5, 1536, 64, 128, False),
     (1, 2, 2048, 128, 128, True),
-    (2, 3, 777, 64, 96, True),
+    (2, 3, 777, 64, 128, True),
 ])
 def test_correction_bit_identical_to_classic(engine, B, H, S, D, BN, ramp):
     """The correction warpgroup does the softmax warps' rescale and epilogue
     arithmetic unchanged, so on unsplit plans both kernels give the same
-    bits, rescales included."""
+    bits, rescales included (on the tiles where the default kernel runs the
+    same four-warp softmax)."""
+    assert same_softmax(D, BN)
     torch = _torch()
     q, k, v = make_inputs(B, H, S, D, torch.float16, seed=5 + S)
     if ramp:
