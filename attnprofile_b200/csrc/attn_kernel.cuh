@@ -302,6 +302,11 @@ constexpr bool kLeanCommits = ATTNPROF_LEAN_COMMITS != 0;
 #define ATTNPROF_W8 1
 #endif
 constexpr bool kW8 = ATTNPROF_W8 != 0;
+// 1: also the D = 128 two-buffer tiles (256 x 64, 256 x 32); 0 (default).
+#ifndef ATTNPROF_W8_D128
+#define ATTNPROF_W8_D128 0
+#endif
+constexpr bool kW8D128 = ATTNPROF_W8_D128 != 0;
 // 1 (default): one FULL wait per step for V_j and K_{j+1} (AttnConfig::KV_JOINT_FULL).
 #ifndef ATTNPROF_JOINT_FULL
 #define ATTNPROF_JOINT_FULL 1
@@ -403,7 +408,6 @@ struct AttnConfig {
   // part of the exponentials go to the FMA pipe (POLY8) and P is published in
   // one piece (C3 at 256 x 96: 631 -> 664 TFLOP/s).  At D = 128 neither helps.
   static constexpr bool EXP_BOUND = NQ == 2 && D == 64 && NQ * (2 * BN + D) <= 512;
-  static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND) ? 2 : 1;
   // W8: those tiles give each Q tile eight softmax warps of 16 rows (the
   // 16-lane tensor-memory forms), so that four softmax warps share each SM
   // sub-partition and its exponential unit instead of two: their softmax
@@ -411,7 +415,9 @@ struct AttnConfig {
   // stream.  (At D = 128 the single issuer's chain makes a step's latency
   // matter, and eight warps per tile measured slower there.)  Whole units
   // only: such launches take no key split.
-  static constexpr bool W8 = kW8 && EXP_BOUND && !PAIR && !CORR;
+  static constexpr bool W8 = kW8 && NQ == 2 && NSBUF == 2 && !PAIR && !CORR && (D == 64 || kW8D128);
+  static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND && !W8) ? 2 : 1;
+
   static constexpr int PSPLIT_QUARTERS = kPsplitQuarters >= 0 ? kPsplitQuarters
                                                               : (BN == 128 ? 3 : 2);
   static constexpr int PSPLIT_CHUNKS =
@@ -518,7 +524,7 @@ struct AttnConfig {
   // with eight warps per tile (C3: 709-711 TFLOP/s against 693-695 at 2 and
   // 696 at 0), none elsewhere.
   static constexpr int POLY8 =
-      kPolyPairsOf8 >= 0 ? kPolyPairsOf8 : (W8 ? 1 : (EXP_BOUND ? 2 : 0));
+      kPolyPairsOf8 >= 0 ? kPolyPairsOf8 : (W8 ? (D == 64 ? 1 : 0) : (EXP_BOUND ? 2 : 0));
   static constexpr int MMA_M = 128 * CTAS;
   static constexpr uint32_t IDESC_S = ptx::idesc_f16(MMA_M, BN, kBF16, false);
   static constexpr uint32_t IDESC_PV = ptx::idesc_f16(MMA_M, D, kBF16, true);
@@ -1385,16 +1391,6 @@ __device__ __forceinline__ void tmem_ld_rows16(uint32_t taddr, uint32_t (&r)[4 *
     ptx::tmem_ld16x256b_x4(taddr + 8 * (NB - 4), *reinterpret_cast<uint32_t(*)[16]>(&r[4 * (NB - 4)]));
 }
 
-template <int NB>
-__device__ __forceinline__ void tmem_st_rows16(uint32_t taddr, const uint32_t (&r)[4 * NB]) {
-#pragma unroll
-  for (int k = 0; k + 8 <= NB; k += 8)
-    ptx::tmem_st16x256b_x8(taddr + 8 * k, *reinterpret_cast<const uint32_t(*)[32]>(&r[4 * k]));
-  if constexpr (NB % 8 == 4)
-    ptx::tmem_st16x256b_x4(taddr + 8 * (NB - 4),
-                           *reinterpret_cast<const uint32_t(*)[16]>(&r[4 * (NB - 4)]));
-}
-
 // P of NB 8-key blocks: 4 NB packed columns, two registers per 4 columns.
 template <int NB>
 __device__ __forceinline__ void tmem_st_p16(uint32_t taddr, const uint32_t (&pk)[2 * NB]) {
@@ -1411,7 +1407,7 @@ __device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* s
                                const CUtensorMap* tmO, const WorkTile& wt, const AttnParams& p,
                                const WaitCtx& w, const Prof<PROFILE>& prof) {
   static_assert(C::NSBUF == 2 && C::PHALVES == 1 && !C::PAIR, "W8 serves two-buffer tiles");
-  static_assert(C::BN % 32 == 0 && C::D % 32 == 0, "");
+  static_assert(C::BN % 32 == 0 && C::D % 64 == 0, "");
   constexpr int NB = C::BN / 8;  // 8-key blocks of S
   constexpr int NO = C::D / 8;   // 8-column blocks of O
   auto bar = [&](int i) { return sbase + C::OFF_BAR + 8u * i; };
@@ -1498,18 +1494,21 @@ __device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* s
                                             static_cast<uint32_t>((j - 1) & 1), w, kSiteODone));
       if (!ok) break;
       ptx::tc_fence_after();
-      uint32_t o[4 * NO];
-      tmem_ld_rows16<NO>(lane_base + o_col, o);
-      ptx::tmem_wait_ld();
-      ptx::reg_fence(o);
+#pragma unroll 1
+      for (int c0 = 0; c0 < NO; c0 += 8) {  // 64 columns of O at a time
+        uint32_t o[32];
+        ptx::tmem_ld16x256b_x8(lane_base + o_col + 8 * c0, o);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence(o);
 #pragma unroll
-      for (int k = 0; k < NO; ++k) {
-        o[4 * k] = __float_as_uint(__uint_as_float(o[4 * k]) * aA);
-        o[4 * k + 1] = __float_as_uint(__uint_as_float(o[4 * k + 1]) * aA);
-        o[4 * k + 2] = __float_as_uint(__uint_as_float(o[4 * k + 2]) * aB);
-        o[4 * k + 3] = __float_as_uint(__uint_as_float(o[4 * k + 3]) * aB);
+        for (int k = 0; k < 8; ++k) {
+          o[4 * k] = __float_as_uint(__uint_as_float(o[4 * k]) * aA);
+          o[4 * k + 1] = __float_as_uint(__uint_as_float(o[4 * k + 1]) * aA);
+          o[4 * k + 2] = __float_as_uint(__uint_as_float(o[4 * k + 2]) * aB);
+          o[4 * k + 3] = __float_as_uint(__uint_as_float(o[4 * k + 3]) * aB);
+        }
+        ptx::tmem_st16x256b_x8(lane_base + o_col + 8 * c0, o);
       }
-      tmem_st_rows16<NO>(lane_base + o_col, o);
     }
     if (rec) {
       prof.stamp(kPhSmMax, sl, 1);
@@ -1581,21 +1580,27 @@ __device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* s
   if (go) {
     ptx::tc_fence_after();
     const float invA = 1.f / lA, invB = 1.f / lB;
-    uint32_t o[4 * NO];
-    tmem_ld_rows16<NO>(lane_base + o_col, o);
-    ptx::tmem_wait_ld();
-    ptx::reg_fence(o);
     // Columns 8k + kc, + 1 of rows rA and rB: one 4-byte value each in the
-    // 128B-swizzled staging tile (the TMA box {64, QROWS}).
+    // 128B-swizzled staging tile (the TMA box {64, QROWS}); 64 columns (one
+    // 128 B block of every row) at a time.
+#pragma unroll 1
+    for (int c0 = 0; c0 < NO; c0 += 8) {
+      uint32_t o[32];
+      ptx::tmem_ld16x256b_x8(lane_base + o_col + 8 * c0, o);
+      ptx::tmem_wait_ld();
+      ptx::reg_fence(o);
+      const int dblk = c0 / 8;
 #pragma unroll
-    for (int k = 0; k < NO; ++k) {
-      const int dblk = (8 * k) / 64, chunk = ((8 * k) % 64) / 8;
-      const uint32_t va = pack2<T>(__uint_as_float(o[4 * k]) * invA, __uint_as_float(o[4 * k + 1]) * invA);
-      const uint32_t vb = pack2<T>(__uint_as_float(o[4 * k + 2]) * invB, __uint_as_float(o[4 * k + 3]) * invB);
-      *reinterpret_cast<uint32_t*>(stage_g + dblk * C::Q_BLK_BYTES + rA * 128 +
-                                   ((chunk ^ (rA & 7)) * 16) + 2 * kc) = va;
-      *reinterpret_cast<uint32_t*>(stage_g + dblk * C::Q_BLK_BYTES + rB * 128 +
-                                   ((chunk ^ (rB & 7)) * 16) + 2 * kc) = vb;
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t va =
+            pack2<T>(__uint_as_float(o[4 * k]) * invA, __uint_as_float(o[4 * k + 1]) * invA);
+        const uint32_t vb =
+            pack2<T>(__uint_as_float(o[4 * k + 2]) * invB, __uint_as_float(o[4 * k + 3]) * invB);
+        *reinterpret_cast<uint32_t*>(stage_g + dblk * C::Q_BLK_BYTES + rA * 128 +
+                                     ((k ^ (rA & 7)) * 16) + 2 * kc) = va;
+        *reinterpret_cast<uint32_t*>(stage_g + dblk * C::Q_BLK_BYTES + rB * 128 +
+                                     ((k ^ (rB & 7)) * 16) + 2 * kc) = vb;
+      }
     }
     ptx::fence_proxy_async_smem();
   }
