@@ -158,3 +158,20 @@ def test_plan_split_rejects_bad_arguments(engine):
     assert L.attn_set_split(5) == engine.ERR["INVALID_ARG"]
     assert L.attn_set_split(-1) == engine.ERR["INVALID_ARG"]
     assert L.attn_set_split(0) == 0
+
+
+def test_work_distribution_setters_reject_bad_modes(engine):
+    """attn_set_schedule takes 0..2 and attn_set_correction 0..1; both leave
+    the previous mode in place on a bad one (checked by setting the default
+    back).  Host-only calls: no GPU needed."""
+    L = engine.lib()
+    for bad in (-1, 3, 100):
+        assert L.attn_set_schedule(bad) == engine.ERR["INVALID_ARG"]
+    for bad in (-1, 2, 7):
+        assert L.attn_set_correction(bad) == engine.ERR["INVALID_ARG"]
+    for ok in (1, 0):
+        assert L.attn_set_correction(ok) == 0
+    for ok in (2, 1, 0):
+        assert L.attn_set_schedule(ok) == 0
+    with pytest.raises(engine.AttnError):
+        engine.set_correction(5)
