@@ -52,10 +52,15 @@ def test_split_parity_f16(engine, oracle_mod, mode, BM, BN, S):
 @pytest.mark.parametrize("mode", [2, 3, 4])
 @pytest.mark.parametrize("D", [64, 128])
 def test_split_parity_bf16(engine, oracle_mod, mode, D):
+    """D = 128 on 256 x 64 (two S buffers), D = 64 on 256 x 128 (one): the
+    D = 64 two-buffer tiles run eight softmax warps and take no key split."""
     torch = _torch()
+    BN = 64 if D == 128 else 128
     q, k, v = make_inputs(2, 2, 1500, D, torch.bfloat16, seed=D + mode)
-    out = run_mode(engine, q, k, v, 256, 64, mode)
-    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=64, dtype=1)
+    out = run_mode(engine, q, k, v, 256, BN, mode)
+    plan = engine.query_split(2, 2, 1500, D, BM=256, BN=BN, dtype=1)  # under the forced mode
+    assert plan["split"] > 1, plan
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN, dtype=1)
     mx, mean = compare(oracle_mod, to_u16(out), ref, 1)
     assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
 
