@@ -194,6 +194,63 @@ def test_padded_layout_reads_and_writes_only_valid_rows(engine, oracle_mod, BM):
     assert mx <= 1.0 and mean <= MEAN_ABS
 
 
+@pytest.mark.parametrize("S", [1, 17, 100, 333, 1000])
+@pytest.mark.parametrize("BN", [96, 64, 32])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_parity_eight_warp_tiles_ragged(engine, oracle_mod, S, BN, dt):
+    """The D = 64 two-buffer tiles (BM = 256; eight softmax warps of 16 rows
+    per Q tile): key columns >= S masked in the 16-lane layout, rows >= S not
+    written, both dtypes."""
+    torch = _torch()
+    dtype = torch.float16 if dt == "f16" else torch.bfloat16
+    q, k, v = make_inputs(2, 3, S, 64, dtype, seed=S + BN)
+    out = run_gpu(engine, q, k, v, 256, BN)
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN, dtype=code(dtype))
+    mx, mean = compare(oracle_mod, to_u16(out), ref, code(dtype))
+    assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.parametrize("BN", [96, 64])
+@pytest.mark.parametrize("ramp", ["up", "down"])
+def test_parity_eight_warp_tiles_moving_row_max(engine, oracle_mod, BN, ramp):
+    """Keys scaled by a ramp (see test_parity_moving_row_max) on the D = 64
+    eight-warp tiles: per-row rescale factors of the two rows a thread holds,
+    applied to O through the 16-lane forms.  V is N(0, 0.5^2) so that O stays
+    below 4, where one f16 ulp is still under the 2e-3 bound."""
+    torch = _torch()
+    S = 2048
+    q, k, v = make_inputs(1, 2, S, 64, torch.float16, seed=31 + BN)
+    r = torch.linspace(0.5, 6.0, S) if ramp == "up" else torch.linspace(6.0, 0.5, S)
+    k = (k.float() * r.view(1, 1, S, 1)).half()
+    v = (v.float() * 0.5).half()
+    out = run_gpu(engine, q, k, v, 256, BN)
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
+    mx, mean = compare(oracle_mod, to_u16(out), ref, 0)
+    assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
+
+
+def test_padded_layout_eight_warp_tile(engine, oracle_mod):
+    """The padded layout on 256 x 96 at D = 64: NaN padding never read, O
+    padding never written."""
+    torch = _torch()
+    B, H, S, D, BN = 2, 2, 300, 64, 96
+    SQO, SKV = 512, 384
+    q, k, v = make_inputs(B, H, S, D, torch.float16, seed=6)
+    Qp = torch.full((B, H, SQO, D), float("nan"), dtype=torch.float16)
+    Kp = torch.full((B, H, SKV, D), float("nan"), dtype=torch.float16)
+    Vp = torch.full((B, H, SKV, D), float("nan"), dtype=torch.float16)
+    Qp[:, :, :S], Kp[:, :, :S], Vp[:, :, :S] = q, k, v
+    Op = torch.full((B, H, SQO, D), 7.0, dtype=torch.float16).cuda()
+    engine.attn_padded(Qp.cuda(), Kp.cuda(), Vp.cuda(), Op, S, BM=256, BN=BN)
+    torch.cuda.synchronize()
+    assert engine.get_status(0)[0] == 0
+    O = Op.cpu()
+    assert torch.all(O[:, :, S:] == 7.0), "padding rows of O were written"
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
+    mx, mean = compare(oracle_mod, to_u16(O[:, :, :S]), ref, 0)
+    assert mx <= 1.0 and mean <= MEAN_ABS
+
+
 def test_constant_v_gives_constant_o(engine):
     """softmax rows sum to one: V = c everywhere gives O = c (up to rounding of c)."""
     torch = _torch()
