@@ -104,7 +104,7 @@ def test_second_reference_oracle_agrees(oracle_mod, path):
     floating-point orders: tuning/utils.cuh:139-198 (pinned bit for bit above)
     and the root driver's verify_attn.cu:4619-4674 (oracle_attn_alt).  On the
     golden inputs they agree within 1e-4 max-abs -- 20x below the kernel's
-    2e-3 tolerance, so the choice of oracle cannot decide a parity verdict."""
+    2e-3 tolerance, so the choice of oracle cannot decide a parity result."""
     z = np.load(path)
     BN = int(z["meta"][5])
     alt = oracle_mod.attention_alt(z["q"], z["k"], z["v"], bn_tile=BN, nthreads=2)
