@@ -12,7 +12,7 @@
 // which tests/test_gpu_ref_verify.py parses.  Its `prop.major < 9` guard
 // passes on a B200 (major 10).
 //
-//   verify_runner <case>    case 0..3, see kCases below; prints the case
+//   verify_runner <case>    case 0..5, see the switch below; prints the case
 //                           line "case B H S D BM BN" then verify_attn's lines
 #include "utils.cuh"
 
@@ -40,8 +40,12 @@ int main(int argc, char** argv) {
     case 1: run_case<1, 1, 512, 128, 128, 64>(1); break;    // one Q tile, narrow key tiles
     case 2: run_case<1, 2, 1000, 128, 256, 128>(2); break;  // ragged: SQO 1024, SKV 1024
     case 3: run_case<2, 2, 300, 64, 256, 96>(3); break;     // D = 64, ragged, padded layout
+    // D = 64 tiles that only the tuning harness builds (wide key tiles, one S
+    // buffer per Q tile): the reference's D = 64 sweep at BM = 256 reaches them.
+    case 4: run_case<1, 2, 1000, 64, 256, 160>(4); break;
+    case 5: run_case<1, 2, 1000, 64, 256, 192>(5); break;
     default:
-      std::fprintf(stderr, "usage: verify_runner <0..3>\n");
+      std::fprintf(stderr, "usage: verify_runner <0..5>\n");
       return 2;
   }
   return 0;

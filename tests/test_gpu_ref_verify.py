@@ -25,7 +25,7 @@ MAX_ABS = 2e-3
 LINE = re.compile(r"max_abs_diff=([0-9.eE+-]+) .* mismatches\(abs>[0-9.]+\)=(\d+)/(\d+)")
 
 
-@pytest.mark.parametrize("case", [0, 1, 2, 3])
+@pytest.mark.parametrize("case", [0, 1, 2, 3, 4, 5])
 def test_reference_verify_attn_accepts_our_runner(case):
     import torch
     if not torch.cuda.is_available():
