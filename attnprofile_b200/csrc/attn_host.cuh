@@ -373,6 +373,11 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   static_assert(CC::SMEM_BYTES <= kSmemLimit, "shared memory over the sm_100 per-CTA limit");
   auto kern_c = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE, PAIR, false, kCorr>;
   const bool corr = kCorr && o.corr;
+  // Eight-warp variants (AttnConfig::W8) store whole units only; their
+  // four-warp kernel runs the launches whose plan splits units along the keys.
+  using C4 = AttnConfig<T, D, BN, NQ, STAGES, PAIR, false, C::W8>;
+  static_assert(C4::SMEM_BYTES <= kSmemLimit, "shared memory over the sm_100 per-CTA limit");
+  auto kern_4 = attn_fwd_kernel<T, D, BN, NQ, STAGES, PROFILE, PAIR, false, false, C::W8>;
   // CTA pairs run as clusters of two consecutive CTAs.
   cudaLaunchAttribute cluster_attr{};
   cluster_attr.id = cudaLaunchAttributeClusterDimension;
@@ -405,7 +410,9 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
           cudaFuncSetAttribute(kern_p, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM_BYTES) != cudaSuccess ||
           cudaFuncSetAttribute(kern_c, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               CC::SMEM_BYTES) != cudaSuccess)
+                               CC::SMEM_BYTES) != cudaSuccess ||
+          cudaFuncSetAttribute(kern_4, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C4::SMEM_BYTES) != cudaSuccess)
         return ATTN_ERR_RESOURCE;
       int sms = 0, occ = 0;
       if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
@@ -430,9 +437,10 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
   // unit per cluster; pairs take no key split).
   const long long qt = (S + C::BM * C::CTAS - 1) / (C::BM * C::CTAS);
   const int n_kv = (S + BN - 1) / BN;
-  // (The correction-warpgroup kernel and the eight-warp tiles store whole
-  // units only: no key split.)
-  SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, (PAIR || corr || C::W8) ? 1 : o.split);
+  // (The correction-warpgroup kernel stores whole units only: no key split.
+  // An eight-warp variant whose plan splits runs its four-warp kernel.)
+  SplitPlan plan = plan_split(BH * qt, n_kv, slots / C::CTAS, (PAIR || corr) ? 1 : o.split);
+  const bool four = C::W8 && plan.split > 1;
   plan_workspace(&plan, C::BM, D, NQ, sizeof(float));
   // Persistent schedule: only when asked for (attn_set_schedule(2)), where
   // the variant has it and the split mode is automatic.  The automatic mode
@@ -521,6 +529,10 @@ int launch_attn(const void* Q, const void* K, const void* V, void* O, int B, int
       if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mo, p) != cudaSuccess) rc = ATTN_ERR_CUDA;
     } else if (corr) {
       kern_c<<<static_cast<unsigned>(plan.ctas), CC::NUM_THREADS, CC::SMEM_BYTES, stream>>>(
+          mq, mk, mv, mo, p);
+      if (cudaGetLastError() != cudaSuccess) rc = ATTN_ERR_CUDA;
+    } else if (four) {
+      kern_4<<<static_cast<unsigned>(plan.ctas), C4::NUM_THREADS, C4::SMEM_BYTES, stream>>>(
           mq, mk, mv, mo, p);
       if (cudaGetLastError() != cudaSuccess) rc = ATTN_ERR_CUDA;
     } else {

@@ -320,7 +320,8 @@ constexpr bool kJointFull = ATTNPROF_JOINT_FULL != 0;
 // keys) and half of every V tile (D/2 columns), so the per-SM shared-memory
 // traffic of the B operands, the TMA writes and the L2 reads halve and the
 // same ring holds twice as many key tiles.  The even CTA issues all MMAs.
-template <typename T, int D_, int BN_, int NQ_, int STAGES_, bool PAIR_ = false, bool CORR_ = false>
+template <typename T, int D_, int BN_, int NQ_, int STAGES_, bool PAIR_ = false, bool CORR_ = false,
+          bool FOUR_ = false>
 struct AttnConfig {
   static constexpr int D = D_;
   static constexpr int BN = BN_;
@@ -415,7 +416,10 @@ struct AttnConfig {
   // stream.  (At D = 128 the single issuer's chain makes a step's latency
   // matter, and eight warps per tile measured slower there.)  Whole units
   // only: such launches take no key split.
-  static constexpr bool W8 = kW8 && NQ == 2 && NSBUF == 2 && !PAIR && !CORR && (D == 64 || kW8D128);
+  // FOUR_: the four-warp kernel of such a tile, which the host runs when
+  // its plan splits units along the keys.
+  static constexpr bool W8 =
+      kW8 && !FOUR_ && NQ == 2 && NSBUF == 2 && !PAIR && !CORR && (D == 64 || kW8D128);
   static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND && !W8) ? 2 : 1;
 
   static constexpr int PSPLIT_QUARTERS = kPsplitQuarters >= 0 ? kPsplitQuarters
@@ -2375,11 +2379,12 @@ __device__ void softmax_role_persistent(int qi, uint32_t tmem, uint32_t sbase, u
 // kernel of its own for the variants that have it (AttnConfig::PERSIST_OK),
 // so that its softmax loop and the classic one are allocated registers
 // separately.  CORR: the classic schedule with a correction warpgroup
-// (AttnConfig::CORR), whole units only.
+// (AttnConfig::CORR), whole units only.  FOUR: four softmax warps per Q tile
+// where the variant would run eight (AttnConfig::W8), for split plans.
 template <typename T, int D, int BN, int NQ, int STAGES, bool PROFILE, bool PAIR = false,
-          bool PERSIST = false, bool CORR = false>
-__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR>::NUM_THREADS,
-                                  AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR>::MIN_CTAS_PER_SM)
+          bool PERSIST = false, bool CORR = false, bool FOUR = false>
+__global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR, FOUR>::NUM_THREADS,
+                                  AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR, FOUR>::MIN_CTAS_PER_SM)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV,
@@ -2389,7 +2394,7 @@ __global__ void __launch_bounds__(AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR>::
 // generic compute_100 PTX (nvcc -arch=sm_100a does) gets an empty kernel there,
 // which a B200 never runs because the sm_100a binary matches it.
 #if defined(__CUDA_ARCH_FEAT_SM100_ALL) || !defined(__CUDA_ARCH__)
-  using C = AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR>;
+  using C = AttnConfig<T, D, BN, NQ, STAGES, PAIR, CORR, FOUR>;
   static_assert(!(CORR && PERSIST), "the correction warpgroup runs the classic schedule");
   constexpr int G = C::CTAS;
   extern __shared__ uint8_t smem_raw[];

@@ -65,6 +65,24 @@ def test_split_parity_bf16(engine, oracle_mod, mode, D):
     assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
 
 
+@pytest.mark.parametrize("mode", [0, 2, 4])
+@pytest.mark.parametrize("BN", [96, 64])
+def test_split_on_eight_warp_tiles(engine, oracle_mod, mode, BN):
+    """The D = 64 two-buffer tiles run eight softmax warps per Q tile for
+    whole units; a launch whose plan splits units along the keys (forced, or
+    automatic on few long units: 1 x 2 x 4096 is 32 units for 148 SMs) runs
+    the tile's four-warp kernel with the split, against the oracle."""
+    torch = _torch()
+    q, k, v = make_inputs(1, 2, 4096, 64, torch.float16, seed=mode + BN)
+    out = run_mode(engine, q, k, v, 256, BN, mode)
+    plan = engine.query_split(1, 2, 4096, 64, BM=256, BN=BN)  # under the same mode
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert plan["split"] > 1, plan
+    ref = oracle_mod.attention(to_u16(q), to_u16(k), to_u16(v), bn_tile=BN)
+    mx, mean = compare(oracle_mod, to_u16(out), ref, 0)
+    assert mx <= 1.0 and mean <= MEAN_ABS, (mx, mean)
+
+
 def test_split_counts_above_the_tile_count_are_clamped(engine, oracle_mod):
     """S = 200 at BN = 128 has two key tiles: a forced 4-way split runs 2 ranges."""
     torch = _torch()
