@@ -127,6 +127,10 @@ void attn_set_timeout_ns(unsigned long long ns);
  * attn_query_config -- launch geometry of a (D, BM, BN, dtype) variant:
  * threads per CTA, dynamic shared memory bytes, TMEM columns allocated and
  * K/V ring depth.  Returns ATTN_ERR_UNSUPPORTED for combinations not built.
+ * The D = 64 tiles with two S buffers per Q tile (BM = 256, BN <= 96) report
+ * their eight-warp kernel (640 threads); their launches that split units
+ * along the keys, and the correction-warpgroup kernel (512), use other
+ * thread counts with the same shared memory layout.
  * Replaces: the reference's resource model (tuning/solver.py:14-95), which
  * the tuning harness uses to filter configurations.
  */
