@@ -459,13 +459,13 @@ def measure(ctx, wl, bm, bn, steps, warmup, preroll_s, seed, keep_sets=False):
     return out
 
 
-def sub_record(ctx, wl, args):
+def sub_record(ctx, wl, args, preroll_s=SUB_PREROLL_S):
     """One sub-record: workload `wl` on its best tile, timed like the main
     line; value = the whole job's FLOPs / the MAX over ranks of the time."""
     from attnprofile_b200 import shard
     bm, bn = best_tile(wl)
     steps = SUB_STEPS[wl]
-    m = measure(ctx, wl, bm, bn, steps, SUB_WARMUP, SUB_PREROLL_S, args.seed)
+    m = measure(ctx, wl, bm, bn, steps, SUB_WARMUP, preroll_s, args.seed)
     S, D = m["S"], m["D"]
     achieved = flops(m["units"], S, D) / (m["ms"] / steps * 1e-3) / 1e12 if m["units"] else 0.0
     clk = m["clocks"] or {}
@@ -631,20 +631,21 @@ def main():
     del sets, m
     torch.cuda.empty_cache()
 
-    # The same workload under the power limit (after a long pre-roll).
+    # Sub-records, after the main line's timing.  First C3 on one GPU, in
+    # the main line's clock regime (its short pre-roll, before anything long
+    # has run); then the same workload under the power limit (after a long
+    # pre-roll); then the sharded configurations (C4, C5) strong-scaled over
+    # the N GPUs, long enough to sit under the power limit themselves.
+    subs = {}
+    if not args.no_sub and n == 1 and args.workload != "c3":
+        subs["c3"] = sub_record(ctx, "c3", args, preroll_s=args.preroll_s)
     sustained = None
     if not args.no_sub:
         sustained = sustained_record(ctx, args)
-
-    # Sub-records, after the main line's timing: the sharded configurations
-    # (C4, C5) strong-scaled over the N GPUs, and C3 on one GPU.
-    subs = {}
     if not args.no_sub:
         for wl in ("c4", "c5"):
             if wl != args.workload:
                 subs.setdefault("sharded", {})[wl] = sub_record(ctx, wl, args)
-        if n == 1 and args.workload != "c3":
-            subs["c3"] = sub_record(ctx, "c3", args)
 
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
