@@ -102,6 +102,31 @@ def test_noalloc_matches_attn_fwd_twice(engine, oracle_mod, B, H, S, dtype):
     _check_oracle_rows(oracle_mod, Q, K, V, O, BN, seed=H)
 
 
+def test_noalloc_on_an_eight_warp_tile_with_a_split_plan(engine, oracle_mod):
+    """1 x 2 x 8192 at D = 64 on 256 x 96: the tile runs eight softmax warps
+    for whole units, and this plan splits, so the launch runs the tile's
+    four-warp kernel with its partials in the fixed scratch.  Equal to
+    attn_fwd, and to the oracle on sampled rows."""
+    torch = _torch()
+    L = _bind(engine)
+    engine.set_split(0)
+    B, H, S, D, BM, BN = 1, 2, 8192, 64, 256, 96
+    plan = engine.query_split(B, H, S, D, BM=BM, BN=BN)
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert plan["split"] > 1, plan
+    assert plan["workspace_bytes"] <= SCRATCH_BYTES
+    Q, K, V = _inputs(B, H, S, D, torch.float16, 64)
+    ref = torch.empty_like(Q)
+    assert _call(L, "attn_fwd", Q, K, V, ref, BM, BN) == 0
+    O = torch.full_like(Q, float("nan"))
+    assert _call(L, "attn_fwd_noalloc", Q, K, V, O, BM, BN) == 0
+    torch.cuda.synchronize()
+    rc, site = engine.get_status(0)
+    assert rc == 0, hex(site)
+    assert torch.equal(O, ref)
+    _check_oracle_rows(oracle_mod, Q, K, V, O, BN)
+
+
 def test_noalloc_unsplit_call_then_split_call(engine):
     """The first call on the device needs no scratch (one whole wave), the
     next one splits: both run, and the second matches attn_fwd."""
