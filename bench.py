@@ -543,6 +543,12 @@ def main():
     achieved = flops(units, S, D) / (per_launch_ms * 1e-3) / 1e12
     burst, sustained, kind = peaks()
     peak = sustained if ms > 1000.0 else burst
+    # Every rank's own rate and clock (the job time is the slowest rank's).
+    ranks = None
+    if n > 1:
+        per = [shard.gather_over_ranks(x, dev) for x in
+               (ms, achieved, (clocks or {}).get("sm_mhz") or 0.0)]
+        ranks = {"ms": per[0], "achieved_tflops": per[1], "sm_mhz": per[2]}
     traffic = None
     tf = ROOT / "profiles" / "ncu_traffic.json"
     if tf.exists():
@@ -669,6 +675,7 @@ def main():
                          "kernel": "attn_fwd_kernel"},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
+            "ranks": ranks,
             "plan": dict(ap.query_split(cfg["B"], w["H"], S, D, BM=args.bm, BN=args.bn,
                                         dtype=0 if w["dtype"] == "f16" else 1),
                          schedule={0: "automatic (classic)", 1: "classic",
