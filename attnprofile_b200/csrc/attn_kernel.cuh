@@ -307,6 +307,11 @@ constexpr bool kW8 = ATTNPROF_W8 != 0;
 #define ATTNPROF_W8_D128 0
 #endif
 constexpr bool kW8D128 = ATTNPROF_W8_D128 != 0;
+// 1: also the D = 64 tile with one S buffer per Q tile (256 x 128); 0 (default).
+#ifndef ATTNPROF_W8_ONE
+#define ATTNPROF_W8_ONE 0
+#endif
+constexpr bool kW8One = ATTNPROF_W8_ONE != 0;
 // 1 (default): one FULL wait per step for V_j and K_{j+1} (AttnConfig::KV_JOINT_FULL).
 #ifndef ATTNPROF_JOINT_FULL
 #define ATTNPROF_JOINT_FULL 1
@@ -376,7 +381,10 @@ struct AttnConfig {
   // buffer each (the next item's first S follows the last P V like any other
   // S) and no CTA pair.  (One-tile CTAs with one S buffer, BN = 256, would
   // spill registers in it.)
-  static constexpr bool PERSIST_OK = NSBUF == 1 && !PAIR && NQ == 2 && !CORR;
+  // (W8_ONE: the D = 64 one-buffer tile that runs eight softmax warps.)
+  static constexpr bool W8_ONE =
+      kW8 && kW8One && !FOUR_ && NQ == 2 && NSBUF == 1 && !PAIR && !CORR && D == 64 && BN <= 128;
+  static constexpr bool PERSIST_OK = NSBUF == 1 && !PAIR && NQ == 2 && !CORR && !W8_ONE;
   // Variants that also have the correction-warpgroup kernel (the tiles of
   // the benchmark configurations).
   static constexpr bool CORR_OK = NQ == 2 && !PAIR && (BN == 128 || (D == 64 && BN == 96));
@@ -419,8 +427,9 @@ struct AttnConfig {
   // FOUR_: the four-warp kernel of such a tile, which the host runs when
   // its plan splits units along the keys.
   static constexpr bool W8 =
-      kW8 && !FOUR_ && NQ == 2 && NSBUF == 2 && !PAIR && !CORR && (D == 64 || kW8D128);
-  static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND && !W8) ? 2 : 1;
+      (kW8 && !FOUR_ && NQ == 2 && NSBUF == 2 && !PAIR && !CORR && (D == 64 || kW8D128)) ||
+      W8_ONE;
+  static constexpr int PHALVES = (BN >= 64 && !EXP_BOUND && !(W8 && NSBUF == 2)) ? 2 : 1;
 
   static constexpr int PSPLIT_QUARTERS = kPsplitQuarters >= 0 ? kPsplitQuarters
                                                               : (BN == 128 ? 3 : 2);
@@ -1395,22 +1404,24 @@ __device__ __forceinline__ void tmem_ld_rows16(uint32_t taddr, uint32_t (&r)[4 *
     ptx::tmem_ld16x256b_x4(taddr + 8 * (NB - 4), *reinterpret_cast<uint32_t(*)[16]>(&r[4 * (NB - 4)]));
 }
 
-// P of NB 8-key blocks: 4 NB packed columns, two registers per 4 columns.
-template <int NB>
+// P of 8-key blocks [K0, K1) of NB: packed columns 4 K0 .. 4 K1 - 1, two
+// registers per 4 columns.
+template <int K0, int K1, int NB>
 __device__ __forceinline__ void tmem_st_p16(uint32_t taddr, const uint32_t (&pk)[2 * NB]) {
+  static_assert((K1 - K0) % 4 == 0, "8-key blocks in multiples of 4");
 #pragma unroll
-  for (int k = 0; k + 8 <= NB; k += 8)
+  for (int k = K0; k + 8 <= K1; k += 8)
     ptx::tmem_st16x128b_x8(taddr + 4 * k, *reinterpret_cast<const uint32_t(*)[16]>(&pk[2 * k]));
-  if constexpr (NB % 8 == 4)
-    ptx::tmem_st16x128b_x4(taddr + 4 * (NB - 4),
-                           *reinterpret_cast<const uint32_t(*)[8]>(&pk[2 * (NB - 4)]));
+  if constexpr ((K1 - K0) % 8 == 4)
+    ptx::tmem_st16x128b_x4(taddr + 4 * (K1 - 4),
+                           *reinterpret_cast<const uint32_t(*)[8]>(&pk[2 * (K1 - 4)]));
 }
 
 template <typename T, class C, bool PROFILE>
 __device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* sgen,
                                const CUtensorMap* tmO, const WorkTile& wt, const AttnParams& p,
                                const WaitCtx& w, const Prof<PROFILE>& prof) {
-  static_assert(C::NSBUF == 2 && C::PHALVES == 1 && !C::PAIR, "W8 serves two-buffer tiles");
+  static_assert(!C::PAIR && (C::NSBUF == 1 || C::PHALVES == 1), "W8 tiles");
   static_assert(C::BN % 32 == 0 && C::D % 64 == 0, "");
   constexpr int NB = C::BN / 8;  // 8-key blocks of S
   constexpr int NO = C::D / 8;   // 8-column blocks of O
@@ -1492,11 +1503,13 @@ __device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* s
       }
     }
     if (__any_sync(0xffffffffu, resc)) {
-      // O holds the sum through P V of step j - 1: wait for it (two S
-      // buffers commit O_DONE every step), then scale in place.
-      ok = __all_sync(0xffffffffu, wait_bar(bar(C::BAR_O_DONE + qi),
-                                            static_cast<uint32_t>((j - 1) & 1), w, kSiteODone));
-      if (!ok) break;
+      // O holds the sum through P V of step j - 1: with two S buffers wait
+      // for its O_DONE; with one, the S_FULL seen above already covers it.
+      if constexpr (C::ODONE_PER_STEP) {
+        ok = __all_sync(0xffffffffu, wait_bar(bar(C::BAR_O_DONE + qi),
+                                              static_cast<uint32_t>((j - 1) & 1), w, kSiteODone));
+        if (!ok) break;
+      }
       ptx::tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < NO; c0 += 8) {  // 64 columns of O at a time
@@ -1527,8 +1540,21 @@ __device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* s
     const float poly_bB = (negB + 126.0f) * (1.0f / 134.0f);
     uint64_t sumA2 = 0ull, sumB2 = 0ull;
     uint32_t pk[2 * NB];
+    // With P in two parts, the first (blocks [0, KB)) is published as soon
+    // as it is in tensor memory.
+    constexpr int KB = C::PHALVES == 2 ? 4 * C::PSPLIT_CHUNKS : NB;
+    const int pbar = C::BAR_P_READY + (qi * C::NSBUF + buf) * C::PHALVES;
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
+      if (C::PHALVES == 2 && k == KB) {
+        tmem_st_p16<0, (C::PHALVES == 2 ? KB : 0), NB>(lane_base + s_col, pk);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(pbar));
+        if (rec) prof.stamp(kPhPFirst, sl, 0);
+        if (rec1) prof.stamp(kPhPFirst, sl, 1);
+      }
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const float s0 = __uint_as_float(sr[4 * k + 2 * r]), s1 = __uint_as_float(sr[4 * k + 2 * r + 1]);
@@ -1549,7 +1575,7 @@ __device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* s
         pk[2 * k + r] = pack2<T>(p0, p1);
       }
     }
-    tmem_st_p16<NB>(lane_base + s_col, pk);
+    tmem_st_p16<(C::PHALVES == 2 ? KB : 0), NB, NB>(lane_base + s_col, pk);
     float s0, s1, s2, s3;
     ptx::f2_unpack(sumA2, s0, s1);
     ptx::f2_unpack(sumB2, s2, s3);
@@ -1561,7 +1587,7 @@ __device__ void softmax_role16(int qi, uint32_t tmem, uint32_t sbase, uint8_t* s
     if (rec) prof.stamp(kPhSmStoreP, sl, 1);
     ptx::tc_fence_before();
     __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(bar(C::BAR_P_READY + (qi * C::NSBUF + buf) * C::PHALVES));
+    if (lane == 0) ptx::mbar_arrive(bar(pbar + C::PHALVES - 1));
     if (rec) prof.stamp(kPhSoftmax, sl, 1);
     if (rec1) prof.stamp(kPhSoftmaxT1, sl, 1);
     lA = lA * aA + (s0 + s1);
